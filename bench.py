@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized MoE W13 grouped GEMM hot path (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload dsv3_decode]
+
+One step = one pass of the W13 path over one batch: routing ids -> expert
+permutation -> gathered per-token FP8 quantization -> FP8 block-scaled grouped
+GEMM (bf16 out).  Default workload: DeepSeek-V3 decode W13 (E=256, top-8
+uniform, 128 tokens, K=7168, N=4096), seeded synthetic data and random-init
+weights.  With N>1 GPUs the same global batch is run expert-parallel
+(E/N experts per GPU, NCCL dispatch/combine): strong scaling.
+
+Prints one JSON line on rank 0.  Timing: W untimed warm-up steps, then K
+steps, each bracketed by CUDA events on the launching stream with a 256 MB
+L2 flush between steps (outside the events); barrier + synchronize around the
+timed region; max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FLUSH_BYTES = 256 << 20
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="dsv3_decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-only", type=int, default=0,
+                    help="profiling aid: run N bare GEMM launches and exit")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for _, _, fl in rows for n, v in zip(names, fl) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def fp8_algorithmic(cfg, counts):
+    """SURVEY-defined algorithmic bytes and FLOPs for the FP8 W13 GEMM."""
+    R = int(sum(counts))
+    active = sum(1 for c in counts if c > 0)
+    n_out = cfg.N // 2 if cfg.silu else cfg.N
+    nk = cfg.K // 128
+    wbytes = active * (cfg.N * cfg.K + (cfg.N // 128) * nk * 4)
+    byts = wbytes + R * cfg.K + R * nk * 4 + R * n_out * 2
+    flops = 2.0 * R * cfg.N * cfg.K
+    return byts, flops, active
+
+
+def read_traffic(kernel_tag):
+    """dram bytes per launch recorded from an ncu capture in profiles/<tag>.md."""
+    path = os.path.join(ROOT, "profiles", f"{kernel_tag}.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_baseline(a_q, a_scale, W, W_s, offsets, cfg, budget_s=12.0, max_experts=64):
+    """The torch CPU fp32 dequantize-then-matmul path on a bounded sample of
+    the same workload: whole experts in order until ~budget_s of CPU work."""
+    import torch
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    counts = (offsets[1:] - offsets[:-1]).tolist()
+    experts = [e for e, c in enumerate(counts) if c > 0][:max_experts]
+    flops = 0.0
+    done = []
+    t0 = time.perf_counter()
+    for e in experts:
+        r0, r1 = int(offsets[e]), int(offsets[e + 1])
+        w_e = W[e:e + 1].cpu()
+        ws_e = W_s[e:e + 1].cpu()
+        off = torch.tensor([0, r1 - r0])
+        t1 = time.perf_counter()
+        O.fp8_w13_torch_cpu(a_q[r0:r1], a_scale[r0:r1], w_e, ws_e, off, [0], silu=cfg.silu)
+        flops += 2.0 * (r1 - r0) * cfg.N * cfg.K
+        done.append((e, time.perf_counter() - t1))
+        if time.perf_counter() - t0 > budget_s:
+            break
+    compute_s = sum(t for _, t in done)
+    rows = sum(int(offsets[e + 1] - offsets[e]) for e, _ in done)
+    return {"value": flops / compute_s / 1e12, "unit": "TFLOPS", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{len(done)} of {sum(1 for c in counts if c > 0)} active experts "
+                      f"({rows} routed rows), torch fp32 dequantize-then-matmul per expert, "
+                      f"{compute_s:.1f} s"}
+
+
+# ---------------------------------------------------------------------------
+# our arm, one GPU
+# ---------------------------------------------------------------------------
+
+def run_single(args, cfg):
+    import torch
+    from ferret_b200 import build, data, ops
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    W, W_s = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K).to(dev)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
+    n_out = cfg.N // 2 if cfg.silu else cfg.N
+    bufs = ops.W13Buffers(cfg.T, cfg.topk, cfg.K, n_out, cfg.E, dev)
+
+    def step():
+        ops.fp8_moe_w13(hidden, ids, W, W_s, silu=cfg.silu, bufs=bufs)
+
+    if args.gemm_only:
+        step()
+        for _ in range(args.gemm_only):
+            ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
+                                                 expert_offsets=bufs.offsets, silu=cfg.silu)
+        torch.cuda.synchronize()
+        return None
+
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ops.last_device_status() != 0:
+        raise RuntimeError("device status error after warm-up")
+
+    def timed(fn, k):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(k)]
+        for i in range(k):
+            flush.zero_()
+            evs[i][0].record(stream)
+            fn()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
+
+    clocks = Clocks(torch.cuda.current_device())
+    torch.cuda.synchronize()
+    clocks.start()
+    step_ms = timed(step, args.steps)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+
+    # dominant kernel alone (same stream, same flush discipline)
+    def gemm():
+        ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
+                                             expert_offsets=bufs.offsets, silu=cfg.silu)
+    gemm_ms = timed(gemm, args.steps)
+
+    # end to end through the public API with host buffers
+    h_hidden = hidden.cpu().pin_memory()
+    h_ids = ids.cpu().pin_memory()
+    h_out = torch.empty(bufs.out.shape, dtype=bufs.out.dtype).pin_memory()
+    d_hidden = torch.empty_like(hidden)
+    d_ids = torch.empty_like(ids)
+
+    def e2e():
+        d_hidden.copy_(h_hidden, non_blocking=True)
+        d_ids.copy_(h_ids, non_blocking=True)
+        out, _, _ = ops.fp8_moe_w13(d_hidden, d_ids, W, W_s, silu=cfg.silu, bufs=bufs)
+        h_out.copy_(out, non_blocking=True)
+    e2e()
+    e2e_ms = timed(e2e, args.steps)
+    if ops.last_device_status() != 0:
+        raise RuntimeError("device status error after timing")
+    out_ok = bool(torch.isfinite(bufs.out[: int(bufs.offsets[-1])].float()).all())
+
+    offsets = bufs.offsets.cpu()
+    counts = (offsets[1:] - offsets[:-1]).tolist()
+    byts, flops, active = fp8_algorithmic(cfg, counts)
+    ms = sum(step_ms) / len(step_ms)
+    g_ms = sum(gemm_ms) / len(gemm_ms)
+    e_ms = sum(e2e_ms) / len(e2e_ms)
+    pk = peaks()
+    achieved = byts / (g_ms * 1e-3) / 1e9
+    res = {
+        "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
+        "value": round(flops / (ms * 1e-3) / 1e12, 3),
+        "unit": "TFLOPS",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
+        "data": "synthetic (seeded), random-init weights",
+        "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
+                   "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
+                   "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
+                   "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
+        "hbm_gbs_step": round(byts / (ms * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "fp8_w13_grouped_kernel",
+                     "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "peak_source": pk["source"] + " (hbm_gbs)",
+                     "algorithmic_bytes": byts, "kernel_ms": round(g_ms, 4),
+                     "kernel_tflops": round(flops / (g_ms * 1e-3) / 1e12, 3),
+                     "traffic": read_traffic(f"fp8_w13_grouped_{cfg.name}")},
+        "e2e": {"value": round(flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+                "ms_per_step": round(e_ms, 4),
+                "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
+                "d2h_bytes_per_step": h_out.numel() * 2},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk,
+        "output_finite": out_ok,
+    }
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(bufs.a.cpu(), bufs.a_scale.cpu(), W, W_s, offsets, cfg)
+    return res
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU fp32 path on the host cores
+# ---------------------------------------------------------------------------
+
+def run_reference(args, cfg):
+    import torch
+    from ferret_b200 import data
+    from oracle import oracle as O
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s)
+    flat = ids.reshape(-1)
+    counts = torch.bincount(flat, minlength=cfg.E)
+    experts = [int(e) for e in torch.nonzero(counts).flatten()]
+    hidden = data.activations(cfg.T, cfg.K)
+    # one step = a bounded sample: SAMPLE experts (all their routed rows)
+    SAMPLE = 4
+    g = torch.Generator().manual_seed(0)
+
+    def expert_inputs(e):
+        rows = torch.nonzero(flat == e).flatten() // cfg.topk
+        w = torch.randn(1, cfg.N, cfg.K, generator=g) * 0.02
+        wq, ws = data.per_block_cast_to_fp8(w)
+        x = hidden[rows].float().view(len(rows), cfg.K // 128, 128)
+        amax = x.abs().amax(dim=2).clamp(min=1e-4)
+        aq = (x * (448.0 / amax.unsqueeze(2))).to(torch.float8_e4m3fn).view(len(rows), cfg.K)
+        return aq, amax / 448.0, wq, ws
+
+    samples = [expert_inputs(e) for e in experts[: SAMPLE * 2]]
+    times, flops = [], []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        f = 0.0
+        for j in range(SAMPLE):
+            aq, as_, wq, ws = samples[(i * SAMPLE + j) % len(samples)]
+            O.fp8_w13_torch_cpu(aq, as_, wq, ws, torch.tensor([0, aq.shape[0]]), [0], silu=cfg.silu)
+            f += 2.0 * aq.shape[0] * cfg.N * cfg.K
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+            flops.append(f)
+    tf = sum(flops) / sum(times) / 1e12
+    ms = 1e3 * sum(times) / len(times)
+    cores = torch.get_num_threads()
+    sample = (f"{SAMPLE} experts per step (all their routed rows) of {len(experts)} active; "
+              "torch fp32 dequantize-then-matmul (correctness/compare_marlin_vs_ref.py:44-100 "
+              "restated for FP8 block scales)")
+    return {
+        "impl": "reference",
+        "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
+        "value": round(tf, 5), "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
+                   "K": cfg.K, "N": cfg.N, "silu": cfg.silu, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOPS", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tf, 5), "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    from ferret_b200.data import CONFIGS
+    cfg = CONFIGS[args.workload]
+    if args.impl == "reference":
+        res = run_reference(args, cfg)
+    elif args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        from ferret_b200 import ep_bench
+        res = ep_bench.run(args, cfg)
+    else:
+        res = run_single(args, cfg)
+    if res is not None and int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,46 @@
+// capi_internal.h -- host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/ferret_moe.h"
+#include "ferret_common.cuh"
+
+namespace ferret {
+
+// Per-device facts resolved once: SM count, shared-memory limit, address of
+// the status word, compute capability.
+struct DeviceInfo {
+    int device = -1;
+    int num_sms = 0;
+    int max_smem_optin = 0;
+    int cc_major = 0, cc_minor = 0;
+    int* status = nullptr;
+};
+
+// Fills `info` for the current device; returns FERRET_OK or an error code.
+int current_device(DeviceInfo** info);
+
+// Builds the DevCtl passed to every kernel launch.
+DevCtl make_ctl(const DeviceInfo* info);
+
+// 2-D tensor map over a row-major [rows, cols] matrix of `elem_bytes`
+// elements with a (box_cols x box_rows) box.  swizzle128 selects the
+// 128-byte swizzle (box_cols * elem_bytes must then be 128).
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_cols,
+                 uint32_t box_rows, bool swizzle128);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Maps a launch error to FERRET_ERR_CUDA (and clears it).
+inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FERRET_OK : FERRET_ERR_CUDA;
+}
+
+}  // namespace ferret

@@ -1,0 +1,179 @@
+"""Torch-facing operators over the C ABI (device tensors in, device tensors out).
+
+The names and argument tuples mirror the reference's baseline call sites so
+the library drops in where they are used:
+
+* ``m_grouped_fp8_gemm_nt_contiguous((A, A_scale), (W, W_scale), out,
+  m_indices, disable_ue8m0_cast=True)`` -- DeepGEMM's grouped FP8 GEMM as
+  called at baselines/fp8-group-gemm/baseline_dsv3_decode.py:55-57.
+* ``per_token_cast_to_fp8(x)`` -- the activation quantizer of
+  baselines/fp8-group-gemm/baseline_dsv3_decode.py:42 (use_ue8m0=False).
+* ``moe_permute(topk_ids, E)`` -- the routing sort the reference takes from
+  vLLM's moe_align_block_size (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126),
+  unpadded: (sorted_rows, expert_offsets, m_indices).
+* ``fp8_moe_w13(hidden, topk_ids, W, W_scale)`` -- the whole W13 hot path:
+  permute -> gathered per-token quantization -> grouped GEMM.
+
+All calls are asynchronous on ``torch.cuda.current_stream()``.  Every op runs
+the CUDA library; there is no CPU or eager-torch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import FERRET_SILU_MUL, FERRET_TILE_SHIFT, check, lib
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t: torch.Tensor, dtype, name: str, ndim: int | None = None):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+
+
+def set_wait_timeout(seconds: float) -> None:
+    check(lib().ferret_set_wait_timeout_ns(int(seconds * 1e9)), "ferret_set_wait_timeout_ns")
+
+
+def last_device_status() -> int:
+    st = ctypes.c_int32(0)
+    check(lib().ferret_last_device_status(_stream(), ctypes.byref(st)), "ferret_last_device_status")
+    return int(st.value)
+
+
+def moe_permute(topk_ids: torch.Tensor, num_experts: int):
+    """topk_ids int32 [T, topk] -> (sorted_rows [T*topk], expert_offsets [E+1], m_indices [T*topk])."""
+    _need(topk_ids, torch.int32, "topk_ids", 2)
+    T, topk = topk_ids.shape
+    dev = topk_ids.device
+    sorted_rows = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    m_indices = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    check(lib().ferret_moe_permute(_ptr(topk_ids), T, topk, num_experts, _ptr(sorted_rows),
+                                   _ptr(offsets), _ptr(m_indices), None, 0, _stream()),
+          "ferret_moe_permute")
+    return sorted_rows, offsets, m_indices
+
+
+def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = None,
+                          gather_div: int = 1, out=None):
+    """bf16 [rows, K] -> (e4m3 [R, K], f32 scales [R, K/128]).  With gather_rows,
+    output row r quantizes x[gather_rows[r] // gather_div] (negative -> zeros)."""
+    _need(x, torch.bfloat16, "x", 2)
+    K = x.shape[1]
+    R = x.shape[0] if gather_rows is None else gather_rows.shape[0]
+    if gather_rows is not None:
+        _need(gather_rows, torch.int32, "gather_rows", 1)
+    if out is None:
+        q = torch.empty(R, K, dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.empty(R, K // 128, dtype=torch.float32, device=x.device)
+    else:
+        q, s = out
+    check(lib().ferret_quant_act_fp8_1x128(_ptr(x), x.shape[0], _ptr(gather_rows), gather_div, R,
+                                           K, _ptr(q), _ptr(s), _stream()),
+          "ferret_quant_act_fp8_1x128")
+    return q, s
+
+
+def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.Tensor | None,
+                                     disable_ue8m0_cast: bool = True,
+                                     expert_offsets: torch.Tensor | None = None,
+                                     silu: bool = False, tile: int = 0) -> None:
+    """out[r] = dequant(A[r]) @ dequant(W[m_indices[r]])^T with exact fp32 block scales.
+
+    ``disable_ue8m0_cast`` is accepted for signature compatibility; scales are
+    always applied in fp32 (never rounded to powers of two).
+    """
+    A, A_scale = a
+    W, W_scale = b
+    if A.dtype == torch.float8_e4m3fn:
+        A = A.view(torch.uint8)
+    if W.dtype == torch.float8_e4m3fn:
+        W = W.view(torch.uint8)
+    _need(A, torch.uint8, "A", 2)
+    _need(W, torch.uint8, "W", 3)
+    _need(A_scale, torch.float32, "A_scale", 2)
+    _need(W_scale, torch.float32, "W_scale", 3)
+    _need(out, torch.bfloat16, "out", 2)
+    M, K = A.shape
+    E, N, K2 = W.shape
+    if K2 != K:
+        raise ValueError("A and W disagree on K")
+    if out.shape != (M, N // 2 if silu else N):
+        raise ValueError(f"out must be [{M}, {N // 2 if silu else N}], got {tuple(out.shape)}")
+    ws = None
+    ws_bytes = 0
+    if expert_offsets is None:
+        _need(m_indices, torch.int32, "m_indices", 1)
+        ws_bytes = lib().ferret_fp8_grouped_gemm_workspace_size(M, E)
+        ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=A.device)
+    else:
+        _need(expert_offsets, torch.int32, "expert_offsets", 1)
+    flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+    check(lib().ferret_fp8_grouped_gemm_nt_contiguous(
+        _ptr(A), _ptr(A_scale), _ptr(W), _ptr(W_scale), _ptr(out), _ptr(m_indices),
+        _ptr(expert_offsets), M, N, K, E, flags, _ptr(ws), ws_bytes, _stream()),
+        "ferret_fp8_grouped_gemm_nt_contiguous")
+
+
+class W13Buffers:
+    """Preallocated intermediates of the fused W13 path for fixed sizes."""
+
+    def __init__(self, T: int, topk: int, K: int, N_out: int, E: int, device):
+        R = T * topk
+        self.sorted_rows = torch.empty(R, dtype=torch.int32, device=device)
+        self.offsets = torch.empty(E + 1, dtype=torch.int32, device=device)
+        self.m_indices = torch.empty(R, dtype=torch.int32, device=device)
+        self.a = torch.empty(R, K, dtype=torch.uint8, device=device)
+        self.a_scale = torch.empty(R, K // 128, dtype=torch.float32, device=device)
+        self.out = torch.empty(R, N_out, dtype=torch.bfloat16, device=device)
+
+
+def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
+                W_scale: torch.Tensor, silu: bool = False, bufs: W13Buffers | None = None,
+                tile: int = 0):
+    """The W13 hot path on one GPU.
+
+    hidden bf16 [T, K], topk_ids int32 [T, topk], W e4m3 [E, N, K],
+    W_scale f32 [E, N/128, K/128].  Returns (out, sorted_rows, expert_offsets):
+    out bf16 [T*topk, N or N/2] in expert-sorted order; row i of out belongs to
+    the (token, slot) pair sorted_rows[i] (= token*topk + slot).
+    """
+    _need(hidden, torch.bfloat16, "hidden", 2)
+    _need(topk_ids, torch.int32, "topk_ids", 2)
+    if W.dtype == torch.float8_e4m3fn:
+        W = W.view(torch.uint8)
+    T, K = hidden.shape
+    topk = topk_ids.shape[1]
+    E, N, _ = W.shape
+    n_out = N // 2 if silu else N
+    if bufs is None:
+        bufs = W13Buffers(T, topk, K, n_out, E, hidden.device)
+    L = lib()
+    s = _stream()
+    R = T * topk
+    check(L.ferret_moe_permute(_ptr(topk_ids), T, topk, E, _ptr(bufs.sorted_rows),
+                               _ptr(bufs.offsets), _ptr(bufs.m_indices), None, 0, s),
+          "ferret_moe_permute")
+    check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K,
+                                       _ptr(bufs.a), _ptr(bufs.a_scale), s),
+          "ferret_quant_act_fp8_1x128")
+    flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+    check(L.ferret_fp8_grouped_gemm_nt_contiguous(
+        _ptr(bufs.a), _ptr(bufs.a_scale), _ptr(W), _ptr(W_scale), _ptr(bufs.out), None,
+        _ptr(bufs.offsets), R, N, K, E, flags, None, 0, s), "ferret_fp8_grouped_gemm_nt_contiguous")
+    return bufs.out, bufs.sorted_rows, bufs.offsets

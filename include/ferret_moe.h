@@ -1,0 +1,137 @@
+/*
+ * ferret_moe.h -- C ABI of the B200 quantized MoE W13 (gate+up) library.
+ *
+ * Conventions (the ctypes shim convention of the reference,
+ * tests/compare_decode_linear.py:103-129): plain device pointers and ints,
+ * caller-owned buffers, the CUDA stream passed as `void*` (NULL = legacy
+ * default stream), every call asynchronous on that stream.  Every entry
+ * point returns 0 on success or a negative FERRET_ERR_* code; nothing throws
+ * across this boundary.  Calls on distinct streams are thread-safe.
+ *
+ * Errors that only the device can see (a bounded wait that ran out, an
+ * expert id >= E, non-contiguous expert rows) are recorded in a per-device
+ * status word; read and clear it with ferret_last_device_status().
+ *
+ * Tensor layouts are the reference's (paths relative to xinhaoc/ferret):
+ *   FP8 contiguous grouped layout   tasks/fp8-group-gemm-dsv3-decode.yaml:18-24
+ *   INT4 compressed-tensors layout  baselines/kimi-moe-w13-int4/baseline_marlin.py:62-89
+ */
+#ifndef FERRET_MOE_H
+#define FERRET_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FERRET_API __attribute__((visibility("default")))
+#else
+#define FERRET_API
+#endif
+
+#define FERRET_MOE_VERSION 1
+
+/* return codes */
+#define FERRET_OK 0
+#define FERRET_ERR_SHAPE (-1)       /* unsupported or inconsistent sizes */
+#define FERRET_ERR_ALIGN (-2)       /* a pointer misses its 16-byte alignment */
+#define FERRET_ERR_NULL (-3)        /* a required pointer is NULL */
+#define FERRET_ERR_CUDA (-4)        /* a CUDA runtime / driver call failed */
+#define FERRET_ERR_TIMEOUT (-5)     /* a device wait ran out (status word) */
+#define FERRET_ERR_NCCL (-6)        /* reserved for the collective layer */
+#define FERRET_ERR_WORKSPACE (-7)   /* workspace missing or too small */
+#define FERRET_ERR_UNSUPPORTED (-8) /* no sm_100 device / feature */
+#define FERRET_ERR_DEVICE (-9)      /* device reported a data error */
+
+/* flags for the GEMM entry points */
+#define FERRET_SILU_MUL 0x1         /* fused SiLU(gate)*up epilogue, N_out = N/2 */
+#define FERRET_TILE_SHIFT 8         /* bits 8-15: force token tile (16,32,64,128); 0 = auto */
+
+/* Library version (FERRET_MOE_VERSION). */
+FERRET_API int ferret_version(void);
+
+/* Human-readable text for a return code. */
+FERRET_API const char* ferret_strerror(int code);
+
+/* Upper bound, in nanoseconds, for any single device-side wait; 0 restores
+ * the default (2 s).  Applies to launches issued after the call. */
+FERRET_API int ferret_set_wait_timeout_ns(unsigned long long ns);
+
+/* Reads and clears the current device's status word (stream-ordered on
+ * `stream`, then synchronises that stream).  *status receives 0 or a device
+ * code: 1 timeout (bits 8-15: wait site), 2 expert id >= E, 3 non-contiguous
+ * expert rows, 4 gather index out of range. */
+FERRET_API int ferret_last_device_status(void* stream, int32_t* status);
+
+/*
+ * Routing -> expert-contiguous permutation (stable counting sort).
+ * Replaces: the routing sort the reference takes from vLLM's
+ *   moe_align_block_size(topk_ids, block, E, ignore_invalid_experts=True)
+ *   (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126) and the
+ *   synthetic m_indices of baselines/fp8-group-gemm/baseline_dsv3_decode.py:50.
+ * topk_ids:       int32 [T*topk] (ids outside [0,E) are dropped)
+ * sorted_rows:    int32 [T*topk] flat source index t*topk+j, grouped by
+ *                 expert, ascending inside an expert; -1 past the valid count
+ * expert_offsets: int32 [E+1] exclusive prefix of the per-expert counts
+ * m_indices:      int32 [T*topk] expert of each sorted row (-1 in the tail)
+ * No workspace is needed (pass NULL, 0).  Limits: E <= 1024.
+ */
+FERRET_API int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int E, int32_t* sorted_rows,
+                       int32_t* expert_offsets, int32_t* m_indices, void* workspace,
+                       size_t ws_bytes, void* stream);
+
+/*
+ * Per-token 1x128 FP8 activation quantization (with optional row gather).
+ * Replaces: DeepGEMM per_token_cast_to_fp8(x, use_ue8m0=False)
+ *   (baselines/fp8-group-gemm/baseline_dsv3_decode.py:42).
+ * x_bf16:      bf16 [x_rows, K]
+ * gather_rows: NULL (row r reads x row r; needs R <= x_rows) or int32 [R]:
+ *              row r reads x row gather_rows[r] / gather_div (negative ->
+ *              zero row, scale 0; a source row >= x_rows is skipped like a
+ *              negative one and reported as device status 4)
+ * a_fp8:       e4m3 [R, K]; a_scale: f32 [R, K/128] row-major
+ * amax is clamped at 1e-4; f = fl(fl(1/amax)*448); q = e4m3_satfinite(fl(x*f));
+ * scale = fl(amax/448).
+ * Limits: K % 128 == 0.
+ */
+FERRET_API int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows, const int32_t* gather_rows,
+                                          int gather_div, int R, int K, void* a_fp8,
+                                          float* a_scale, void* stream);
+
+/*
+ * FP8 block-scaled grouped GEMM, contiguous layout, W13 (gate+up).
+ * Replaces: DeepGEMM m_grouped_fp8_gemm_nt_contiguous((A, A_scale),
+ *   (W, W_scale), out, m_indices, disable_ue8m0_cast=True)
+ *   (baselines/fp8-group-gemm/baseline_dsv3_decode.py:55-57,68-70) and the
+ *   reference kernel launcher launch_grouped_gemm_bs
+ *   (examples/fp8-group-gemm/v007_dsv3_decode_verified_105.cu:373-439).
+ * a_fp8 [M,K] e4m3, a_scale [M,K/128] f32, w_fp8 [E,N,K] e4m3,
+ * w_scale [E,N/128,K/128] f32, out_bf16 [M,N] (or [M,N/2] with
+ * FERRET_SILU_MUL: out = silu(x[:, :N/2]) * x[:, N/2:]).
+ * Rows of one expert must be contiguous; rows with m_indices < 0 are padding
+ * and their output rows are not written.
+ * expert_offsets: NULL -> the expert segments are derived on the device from
+ *   m_indices (needs ferret_fp8_grouped_gemm_workspace_size() bytes of
+ *   workspace); non-NULL int32 [E+1] -> rows [off[e], off[e+1]) belong to
+ *   expert e (m_indices is then not read and may be NULL).
+ * Limits: K % 128 == 0, N % 128 == 0 (N % 256 == 0 with SILU), E <= 1024,
+ *   K <= 16384; pointers 16-byte aligned.
+ */
+FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous(const void* a_fp8, const float* a_scale, const void* w_fp8,
+                                          const float* w_scale, void* out_bf16,
+                                          const int32_t* m_indices, const int32_t* expert_offsets,
+                                          int M, int N, int K, int E, int flags, void* workspace,
+                                          size_t ws_bytes, void* stream);
+
+/* Workspace bytes ferret_fp8_grouped_gemm_nt_contiguous needs when
+ * expert_offsets is NULL. */
+FERRET_API size_t ferret_fp8_grouped_gemm_workspace_size(int M, int E);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FERRET_MOE_H */

@@ -1,0 +1,256 @@
+"""GPU parity tests of the FP8 W13 path against the CPU oracle.
+
+Integer outputs (permutation, quantized activations and their scales) must be
+bit-exact.  GEMM outputs are bf16 and must match the fp32 oracle within max
+relative error < 1e-2 (denominator max(|ref|, 1e-3 * max|ref|)), with no NaN,
+over every row (the reference's check at
+examples/fp8-group-gemm/v007_dsv3_decode_verified_105.cu:547-551 and
+tasks/fp8-group-gemm-dsv3-decode.yaml:101, extended from 32 rows to all).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+BF16_NAN = 0x7FFF
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    from ferret_b200 import ops as _ops
+    return _ops
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.uint8).cpu().numpy()
+
+
+# ---------------------------------------------------------------- permutation
+
+@pytest.mark.parametrize("T,topk,E,lo,hi", [
+    (1, 1, 1, 0, 1), (128, 8, 256, 0, 256), (64, 8, 384, 0, 384), (7, 3, 5, -2, 7),
+    (300, 2, 8, 0, 8), (0, 8, 16, 0, 16), (4096, 8, 1024, -1, 1024), (32768, 8, 256, 0, 256),
+    (1000, 4, 3, 2, 3),     # a single expert receives everything
+])
+def test_permute_bit_exact(ops, T, topk, E, lo, hi):
+    rng = np.random.default_rng(T + 7 * E)
+    ids = rng.integers(lo, hi, size=(T, topk)).astype(np.int32)
+    d_rows, d_offs, d_mi = ops.moe_permute(torch.from_numpy(ids).cuda(), E)
+    rows, offs, mi = O.moe_permute(ids, E)
+    assert np.array_equal(d_offs.cpu().numpy(), offs)
+    assert np.array_equal(d_rows.cpu().numpy(), rows)
+    assert np.array_equal(d_mi.cpu().numpy(), mi)
+
+
+# ---------------------------------------------------------------- quantization
+
+@pytest.mark.parametrize("R,K", [(1, 128), (37, 512), (1024, 7168)])
+def test_quant_bit_exact(ops, R, K):
+    g = torch.Generator().manual_seed(R)
+    x = (torch.randn(R, K, generator=g) * torch.logspace(-5, 2, R).unsqueeze(1)).to(torch.bfloat16)
+    x[0, :128] = 0
+    q, s = ops.per_token_cast_to_fp8(x.cuda())
+    qr, sr = O.quant_act_fp8_1x128(u16(x))
+    assert np.array_equal(u8(q), qr)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+
+
+def test_quant_gather_bit_exact(ops):
+    g = torch.Generator().manual_seed(1)
+    T, topk, K = 33, 4, 1024
+    x = torch.randn(T, K, generator=g).to(torch.bfloat16)
+    rows = torch.randperm(T * topk, generator=g).to(torch.int32)
+    rows[-5:] = -1
+    q, s = ops.per_token_cast_to_fp8(x.cuda(), rows.cuda(), topk)
+    qr, sr = O.quant_act_fp8_1x128(u16(x), rows.numpy(), topk)
+    assert np.array_equal(u8(q), qr)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+
+
+def test_quant_matches_torch_cuda_published_algorithm(ops):
+    """The published per_token_cast_to_fp8 evaluated by torch on this GPU."""
+    g = torch.Generator().manual_seed(2)
+    x = (torch.randn(64, 2048, generator=g) * 3).to(torch.bfloat16).cuda()
+    v = x.view(64, -1, 128)
+    amax = v.abs().float().amax(dim=2).view(64, -1).clamp(1e-4)
+    q_ref = (v * (448.0 / amax.unsqueeze(2))).to(torch.float8_e4m3fn).view(64, 2048)
+    q, s = ops.per_token_cast_to_fp8(x)
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8))
+    # torch may evaluate amax / 448 as amax * (1/448) on the GPU: allow 1 ulp
+    s_ref = (amax / 448.0)
+    ulp = (s.view(torch.int32) - s_ref.view(torch.int32)).abs().max().item()
+    assert ulp <= 1
+
+
+# ---------------------------------------------------------------- grouped GEMM
+
+def make_case(seed, seg_counts, N, K, pad_between=0, scale_kind="random"):
+    """Contiguous-layout inputs: experts in order with `pad_between` padding
+    rows (m_indices = -1) after every segment."""
+    rng = np.random.default_rng(seed)
+    E = len(seg_counts)
+    mi = []
+    for e, c in enumerate(seg_counts):
+        mi += [e] * c + [-1] * pad_between
+    mi = np.array(mi, np.int32)
+    M = len(mi)
+    a = O.f32_to_e4m3(rng.standard_normal((M, K)).astype(np.float32) * 100)
+    w = O.f32_to_e4m3(rng.standard_normal((E, N, K)).astype(np.float32) * 100)
+    if scale_kind == "pow2":
+        a_s = np.ldexp(1.0, rng.integers(-12, -6, (M, K // 128))).astype(np.float32)
+        w_s = np.ldexp(1.0, rng.integers(-12, -6, (E, N // 128, K // 128))).astype(np.float32)
+    else:
+        a_s = rng.uniform(1e-3, 1e-2, (M, K // 128)).astype(np.float32)
+        w_s = rng.uniform(1e-4, 1e-3, (E, N // 128, K // 128)).astype(np.float32)
+    return a, a_s, w, w_s, mi
+
+
+def run_gemm(ops, a, a_s, w, w_s, mi, silu, tile, use_offsets):
+    M, K = a.shape
+    E, N, _ = w.shape
+    n_out = N // 2 if silu else N
+    out = torch.full((M, n_out), BF16_NAN, dtype=torch.int16).view(torch.bfloat16).cuda()
+    offs = None
+    if use_offsets:
+        assert (mi >= 0).all()
+        offs = torch.from_numpy(np.concatenate([[0], np.cumsum(np.bincount(mi, minlength=E))])
+                                .astype(np.int32)).cuda()
+    ops.m_grouped_fp8_gemm_nt_contiguous(
+        (torch.from_numpy(a).cuda(), torch.from_numpy(a_s).cuda()),
+        (torch.from_numpy(w).cuda(), torch.from_numpy(w_s).cuda()),
+        out, None if use_offsets else torch.from_numpy(mi).cuda(),
+        expert_offsets=offs, silu=silu, tile=tile)
+    torch.cuda.synchronize()
+    assert ops.last_device_status() == 0
+    return out
+
+
+def check(out, ref, mi):
+    got = O.bf16_to_f32(u16(out))
+    valid = mi >= 0
+    err = O.rel_err(got[valid], ref[valid])
+    assert err["nan"] == 0 and err["max_rel"] < TOL, err
+    # padding rows are never written
+    assert (u16(out)[~valid] == BF16_NAN).all()
+
+
+CASES = [
+    # (seg_counts, N, K, pad, silu, tile)
+    ([5, 0, 17, 1, 3], 256, 256, 0, False, 16),
+    ([5, 0, 17, 1, 3], 256, 256, 0, True, 16),
+    ([40, 3, 0, 70], 512, 384, 0, False, 32),
+    ([40, 3, 0, 70], 512, 384, 0, True, 32),
+    ([130, 64, 1], 256, 512, 0, False, 64),
+    ([130, 64, 1], 512, 512, 0, True, 64),
+    ([300, 129, 2], 384, 256, 0, False, 128),
+    ([1] * 12, 256, 1024, 0, False, 0),
+    ([8, 8, 8, 8], 256, 128, 5, False, 16),     # DeepGEMM-style padding rows
+    ([8, 8, 8, 8], 256, 128, 5, True, 0),
+]
+
+
+@pytest.mark.parametrize("seg,N,K,pad,silu,tile", CASES)
+@pytest.mark.parametrize("use_offsets", [False, True])
+def test_grouped_gemm_vs_oracle(ops, seg, N, K, pad, silu, tile, use_offsets):
+    if use_offsets and pad:
+        pytest.skip("offsets describe unpadded layouts")
+    a, a_s, w, w_s, mi = make_case(hash((tuple(seg), N, K)) & 0xFFFF, seg, N, K, pad)
+    out = run_gemm(ops, a, a_s, w, w_s, mi, silu, tile, use_offsets)
+    ref = O.fp8_grouped_gemm(a, a_s, w, w_s, mi, silu=silu)
+    check(out, ref, mi)
+
+
+def test_grouped_gemm_reference_golden(ops):
+    """The inputs/outputs of the reference's own cpu_ref_bs (tests/golden)."""
+    d = np.load(os.path.join(GOLD, "fp8_v007_ref.npz"))
+    out = run_gemm(ops, d["a"], d["a_scale"], d["w"], d["w_scale"], d["m_indices"], False, 0, False)
+    check(out, d["out"], d["m_indices"])
+
+
+def test_grouped_gemm_is_deterministic(ops):
+    a, a_s, w, w_s, mi = make_case(3, [33, 2, 90], 512, 512)
+    o1 = run_gemm(ops, a, a_s, w, w_s, mi, False, 0, False)
+    o2 = run_gemm(ops, a, a_s, w, w_s, mi, False, 0, False)
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+
+
+def test_grouped_gemm_reports_noncontiguous_rows(ops):
+    a, a_s, w, w_s, _ = make_case(4, [4, 4], 256, 128)
+    mi = np.array([0, 0, 1, 1, 0, 0, 1, 1], np.int32)
+    run_gemm_status = None
+    M, K = a.shape
+    out = torch.empty(M, 256, dtype=torch.bfloat16, device="cuda")
+    ops.m_grouped_fp8_gemm_nt_contiguous(
+        (torch.from_numpy(a).cuda(), torch.from_numpy(a_s).cuda()),
+        (torch.from_numpy(w).cuda(), torch.from_numpy(w_s).cuda()), out,
+        torch.from_numpy(mi).cuda())
+    torch.cuda.synchronize()
+    run_gemm_status = ops.last_device_status()
+    assert run_gemm_status == 3
+    assert ops.last_device_status() == 0   # read-and-clear
+
+
+# ---------------------------------------------------------------- whole W13 path
+
+def oracle_w13(hidden, ids, w, w_s, E, silu):
+    rows, offs, mi = O.moe_permute(ids, E)
+    R = int(offs[-1])
+    q, s = O.quant_act_fp8_1x128(hidden, rows[:R], ids.shape[1])
+    return O.fp8_grouped_gemm(q, s, w, w_s, mi[:R], silu=silu), rows, offs, q, s
+
+
+@pytest.mark.parametrize("silu", [False, True])
+def test_w13_path_cpu_config(ops, silu):
+    """BASELINE config 1 (E=8, top-2 uniform, 256 tokens, K=512, N=1024), all rows."""
+    from ferret_b200 import data
+    cfg = data.CONFIGS["cpu_fp8"]
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K)
+    hidden = data.activations(cfg.T, cfg.K)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk)
+    out, rows, offs = ops.fp8_moe_w13(hidden.cuda(), ids.cuda(), W.cuda(), Ws.cuda(), silu=silu)
+    torch.cuda.synchronize()
+    ref, r_rows, r_offs, _, _ = oracle_w13(u16(hidden), ids.numpy(), u8(W), Ws.numpy(), cfg.E, silu)
+    assert np.array_equal(rows.cpu().numpy(), r_rows)
+    assert np.array_equal(offs.cpu().numpy(), r_offs)
+    err = O.rel_err(O.bf16_to_f32(u16(out)), ref)
+    assert err["nan"] == 0 and err["max_rel"] < TOL, err
+
+
+def test_w13_path_dsv3_decode_full_size(ops):
+    """BASELINE config 2 at full size; every output row of 48 sampled experts
+    is checked against the fp32 oracle, permutation and quantization in full."""
+    from ferret_b200 import data
+    cfg = data.CONFIGS["dsv3_decode"]
+    dev = torch.device("cuda")
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk)
+    out, rows, offs = ops.fp8_moe_w13(hidden.cuda(), ids.cuda(), W, Ws)
+    torch.cuda.synchronize()
+    r_rows, r_offs, r_mi = O.moe_permute(ids.numpy(), cfg.E)
+    assert np.array_equal(rows.cpu().numpy(), r_rows)
+    assert np.array_equal(offs.cpu().numpy(), r_offs)
+    q, s = O.quant_act_fp8_1x128(u16(hidden), r_rows, cfg.topk)
+    qd, sd = ops.per_token_cast_to_fp8(hidden.cuda(), rows, cfg.topk)
+    assert np.array_equal(u8(qd), q)
+    rng = np.random.default_rng(0)
+    experts = rng.choice(np.nonzero(np.diff(r_offs))[0], 48, replace=False)
+    got = O.bf16_to_f32(u16(out))
+    for e in experts:
+        r0, r1 = r_offs[e], r_offs[e + 1]
+        ref = O.fp8_grouped_gemm_fast(q[r0:r1], s[r0:r1], u8(W[e:e + 1]), Ws[e:e + 1].cpu().numpy(),
+                                      np.zeros(r1 - r0, np.int32))
+        err = O.rel_err(got[r0:r1], ref)
+        assert err["nan"] == 0 and err["max_rel"] < TOL, (int(e), err)
+    assert ops.last_device_status() == 0
