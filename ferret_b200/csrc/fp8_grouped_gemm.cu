@@ -520,3 +520,88 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
     }
 #undef FERRET_FP8_CASE
 }
+
+#include <mutex>
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Callers such as a serving process that hands nearly all HBM to weights and
+// the KV cache up front, or a plugin host that binds this library through an
+// FFI and has no handle on the framework's allocator, cannot obtain a
+// workspace at call time.  This entry point keeps the derived expert segments
+// in a fixed device array instead, so it needs no workspace and calls no
+// allocator.  The array lives in this library's module on every GPU that
+// loads the library, until the process exits.
+// ---------------------------------------------------------------------------
+namespace ferret {
+namespace {
+
+constexpr int kNoAllocMaxExperts = kMaxE;                       // 1024 experts
+static __device__ __align__(256) int32_t g_noalloc_segments[2 * kNoAllocMaxExperts];  // 8 KB
+
+constexpr int kNoAllocMaxDevices = 64;
+int32_t* g_noalloc_ptr[kNoAllocMaxDevices];
+int g_noalloc_err[kNoAllocMaxDevices];
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+
+// Runs once per device, with that device current: host code only ever sees a
+// host-side stand-in for the array, so its device address must be queried.
+void noalloc_setup(int dev) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_segments);
+    if (e != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        g_noalloc_err[dev] = FERRET_ERR_CUDA;
+        return;
+    }
+    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
+    g_noalloc_err[dev] = FERRET_OK;
+}
+
+}  // namespace
+}  // namespace ferret
+
+extern "C" int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
+    const void* a_fp8, const float* a_scale, const void* w_fp8, const float* w_scale,
+    void* out_bf16, const int32_t* m_indices, int M, int N, int K, int E, int flags,
+    void* stream) {
+    const bool pair = (flags & FERRET_SILU_MUL) != 0;
+    if (M < 0 || N <= 0 || K <= 0 || E <= 0) return FERRET_ERR_SHAPE;
+    if (E > kNoAllocMaxExperts) return FERRET_ERR_SHAPE;   // beyond the fixed scratch
+    if (K % 128 || N % 128 || (pair && N % 256) || K / 128 > kMaxNK) return FERRET_ERR_SHAPE;
+    if ((long long)E * N >= (1ll << 31) || (long long)M * K >= (1ll << 40)) return FERRET_ERR_SHAPE;
+    if (M == 0) return FERRET_OK;
+    if (!a_fp8 || !a_scale || !w_fp8 || !w_scale || !out_bf16 || !m_indices) return FERRET_ERR_NULL;
+    if (!aligned16(a_fp8) || !aligned16(w_fp8) || !aligned16(out_bf16) ||
+        (reinterpret_cast<uintptr_t>(a_scale) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u))
+        return FERRET_ERR_ALIGN;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    if (info->device < 0 || info->device >= kNoAllocMaxDevices) return FERRET_ERR_UNSUPPORTED;
+    std::call_once(g_noalloc_once[info->device], noalloc_setup, info->device);
+    if (g_noalloc_err[info->device] != FERRET_OK) return g_noalloc_err[info->device];
+    int32_t* seg = g_noalloc_ptr[info->device];
+    cudaStream_t s = as_stream(stream);
+    // every call rewrites all 2E (start, count) entries before the GEMM reads them
+    derive_segments_kernel<<<1, kSegThreads, 3 * E * (int)sizeof(int), s>>>(m_indices, M, E, seg,
+                                                                           make_ctl(info));
+    if ((rc = launch_status()) != FERRET_OK) return rc;
+    const int nt = pick_tile(M, E, flags, pair);
+    switch (nt) {
+        case 16:
+            return pair ? launch_fp8<16, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s)
+                        : launch_fp8<16, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
+        case 32:
+            return pair ? launch_fp8<32, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s)
+                        : launch_fp8<32, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
+        case 64:
+            return pair ? launch_fp8<64, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s)
+                        : launch_fp8<64, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
+        case 128:
+            return launch_fp8<128, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
+        default:
+            return FERRET_ERR_SHAPE;
+    }
+}

@@ -46,6 +46,10 @@ CONFIGS = {
     "kimi_int4_decode": W13Config("kimi_int4_decode", E=384, topk=8, T=64, K=7168, N=4096,
                                   quant="int4"),
     "ep_prefill": W13Config("ep_prefill", E=256, topk=8, T=32768, K=7168, N=4096, routing="zipf"),
+    # one EP=8 rank of the decode config (32 local experts, ~4 rows each): the
+    # reference's own per-rank decode shape (tasks/fp8-group-gemm-dsv3-decode.yaml:14),
+    # also the small case for ncu captures (0.94 GB of weights > L2)
+    "dsv3_decode_rank": W13Config("dsv3_decode_rank", E=32, topk=8, T=16, K=7168, N=4096),
 }
 
 

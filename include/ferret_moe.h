@@ -130,6 +130,28 @@ FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous(const void* a_fp8, const fl
  * expert_offsets is NULL. */
 FERRET_API size_t ferret_fp8_grouped_gemm_workspace_size(int M, int E);
 
+/*
+ * Allocation-free variant of ferret_fp8_grouped_gemm_nt_contiguous (m_indices
+ * form).  No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory when they call -- a serving process that has handed
+ * almost all HBM to weights and the KV cache, or a plugin host that reaches
+ * this library through an FFI and has no access to its framework's allocator.
+ * Same arguments and results as the workspace entry point with
+ * expert_offsets = NULL, minus the workspace: the per-expert segments derived
+ * from m_indices live in a fixed 8 KB device array inside this library
+ * (2 x 1024 int32), which every GPU that loads the library keeps until the
+ * process exits.  It allocates nothing and calls no allocator.
+ * Limit: E <= 1024 (the array's size); larger E returns FERRET_ERR_SHAPE.
+ * The first call on a device looks up the array's device address with that
+ * device current; make that first call before any stream capture.
+ * All calls share the one array and each call rewrites the entries it uses
+ * before reading them; calls that overlap on the GPU (e.g. on two streams at
+ * once) race on it and must be serialised by the caller.
+ */
+FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
+    const void* a_fp8, const float* a_scale, const void* w_fp8, const float* w_scale,
+    void* out_bf16, const int32_t* m_indices, int M, int N, int K, int E, int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
