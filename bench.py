@@ -43,6 +43,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="dsv3_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", choices=["contiguous", "balanced"], default="contiguous",
+                    help="expert placement for N>1 (balanced = greedy LPT on the routing histogram)")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="profiling aid: run N bare GEMM launches and exit")
     return ap.parse_args()

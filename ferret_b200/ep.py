@@ -1,0 +1,164 @@
+"""Expert parallelism for the W13 path: experts sharded over ranks, tokens
+dispatched to the rank that owns their expert and the W13 outputs combined
+back to the token's rank, over torch.distributed (NCCL over NVLink on B200;
+gloo on CPU for the host-logic tests).
+
+One rank per GPU.  Rank r owns E/G experts (contiguous ids by default, or a
+placement table, e.g. the balanced one from ``balanced_placement``) and only
+holds their weights.  A forward step on every rank:
+
+  1. remap expert ids to placement order and permute the local (token, slot)
+     pairs by expert -- expert-sorted order is also destination-rank order;
+  2. all_to_all of the per-expert counts (E ints), one device->host copy of
+     the counts to size the variable splits;
+  3. dispatch all_to_all of the bf16 token rows;
+  4. locally: permute the received rows by local expert, gathered FP8
+     quantization, grouped GEMM (the CUDA kernels);
+  5. un-permute, combine all_to_all back, scatter into (token, slot) order.
+
+The reference has no multi-GPU implementation of this path; parity is the
+single-GPU result for every (token, slot) pair.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+class CudaKernels:
+    """The product kernels (CUDA library via ferret_b200.ops)."""
+
+    def __init__(self):
+        from . import ops
+        self.ops = ops
+
+    def permute(self, ids: torch.Tensor, E: int):
+        rows, offs, _ = self.ops.moe_permute(ids, E)
+        return rows, offs
+
+    def quant(self, x: torch.Tensor, rows: torch.Tensor, div: int):
+        return self.ops.per_token_cast_to_fp8(x, rows, div)
+
+    def gemm(self, q, s, W, Ws, offsets, silu: bool):
+        E, N, _ = W.shape
+        out = torch.empty(q.shape[0], N // 2 if silu else N, dtype=torch.bfloat16, device=q.device)
+        if q.shape[0]:
+            self.ops.m_grouped_fp8_gemm_nt_contiguous((q, s), (W, Ws), out, None,
+                                                      expert_offsets=offsets, silu=silu)
+        return out
+
+
+def contiguous_placement(E: int, G: int) -> torch.Tensor:
+    """owner-order table: slot i (rank i // (E/G)) holds expert table[i]."""
+    return torch.arange(E, dtype=torch.int32)
+
+
+def balanced_placement(counts: torch.Tensor, G: int) -> torch.Tensor:
+    """Greedy LPT with exactly E/G experts per rank: experts by descending load,
+    each to the least-loaded rank that still has room.  Returns the owner-order
+    table (the experts of rank 0, then rank 1, ...)."""
+    E = counts.numel()
+    per = E // G
+    order = torch.argsort(counts.to(torch.int64), descending=True, stable=True).tolist()
+    load = [0] * G
+    slots = [[] for _ in range(G)]
+    for e in order:
+        r = min((g for g in range(G) if len(slots[g]) < per), key=lambda g: (load[g], g))
+        slots[r].append(e)
+        load[r] += int(counts[e])
+    return torch.tensor([e for s in slots for e in sorted(s)], dtype=torch.int32)
+
+
+@dataclass
+class StepTimers:
+    """Optional CUDA events recorded around the local GEMM of a step."""
+    gemm_start: torch.cuda.Event | None = None
+    gemm_end: torch.cuda.Event | None = None
+
+
+class ExpertParallelW13:
+    """W13 forward with experts sharded over the ranks of `group`.
+
+    W_local / Ws_local: this rank's experts, in placement order
+    ([E/G, N, K] e4m3 and [E/G, N/128, K/128] f32); `placement` is the
+    owner-order table (global expert id of every slot; default identity).
+    """
+
+    def __init__(self, W_local, Ws_local, E: int, group=None, silu: bool = False,
+                 placement: torch.Tensor | None = None, kernels=None):
+        self.group = group
+        self.G = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if E % self.G:
+            raise ValueError(f"E={E} must be divisible by the world size {self.G}")
+        self.E, self.El = E, E // self.G
+        if W_local.shape[0] != self.El:
+            raise ValueError(f"W_local holds {W_local.shape[0]} experts, expected {self.El}")
+        self.W, self.Ws, self.silu = W_local, Ws_local, silu
+        self.kernels = kernels or CudaKernels()
+        dev = W_local.device
+        if placement is None:
+            self.remap = None
+        else:
+            # global expert id -> slot in owner order
+            inv = torch.empty(E, dtype=torch.int32)
+            inv[placement.long()] = torch.arange(E, dtype=torch.int32)
+            self.remap = inv.to(dev)
+        self.loc_pattern = torch.arange(self.El, dtype=torch.int32, device=dev).repeat(self.G)
+
+    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+        if self.G == 1:
+            out.copy_(inp)
+            return
+        if out.dtype == torch.bfloat16:
+            # a pure byte copy: move bf16 rows as uint8 so every backend takes them
+            out = out.view(torch.uint8)
+            inp = inp.view(torch.uint8)
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
+                timers: StepTimers | None = None) -> torch.Tensor:
+        """hidden bf16 [T, K], topk_ids int32 [T, topk] (global expert ids) ->
+        bf16 [T*topk, N or N/2] in (token, slot) order; pairs with an invalid
+        expert id get zero rows."""
+        T, topk = topk_ids.shape
+        K = hidden.shape[1]
+        N = self.W.shape[1]
+        n_out = N // 2 if self.silu else N
+        dev = hidden.device
+        ids = topk_ids
+        if self.remap is not None:
+            valid = (ids >= 0) & (ids < self.E)
+            ids = torch.where(valid, self.remap[ids.clamp(0, self.E - 1).long()], -1).to(torch.int32)
+        rows, offs = self.kernels.permute(ids.contiguous(), self.E)
+        counts = (offs[1:] - offs[:-1]).contiguous()
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts)
+        both = torch.cat([counts, recv_counts]).cpu()          # the one host sync
+        send_splits = both[: self.E].view(self.G, self.El).sum(1).tolist()
+        recv_splits = both[self.E:].view(self.G, self.El).sum(1).tolist()
+        Rv, Rr = sum(send_splits), sum(recv_splits)
+
+        sel = rows[:Rv].long()
+        send = hidden.index_select(0, sel // topk)
+        recv = torch.empty(Rr, K, dtype=hidden.dtype, device=dev)
+        self._a2a(recv, send, recv_splits, send_splits)
+
+        loc_ids = torch.repeat_interleave(self.loc_pattern, recv_counts.to(torch.int64),
+                                          output_size=Rr).view(Rr, 1)
+        rows2, offs2 = self.kernels.permute(loc_ids.contiguous(), self.El)
+        q, s = self.kernels.quant(recv, rows2, 1)
+        if timers is not None and timers.gemm_start is not None:
+            timers.gemm_start.record()
+        out2 = self.kernels.gemm(q, s, self.W, self.Ws, offs2, self.silu)
+        if timers is not None and timers.gemm_end is not None:
+            timers.gemm_end.record()
+        back = torch.empty_like(out2)
+        back.index_copy_(0, rows2[:Rr].long(), out2)
+        ret = torch.empty(Rv, n_out, dtype=out2.dtype, device=dev)
+        self._a2a(ret, back, send_splits, recv_splits)
+        out = torch.zeros(T * topk, n_out, dtype=ret.dtype, device=dev)
+        out.index_copy_(0, sel, ret)
+        return out

@@ -1,0 +1,164 @@
+"""Multi-GPU leg of bench.py: the same global W13 batch run expert-parallel.
+
+Launched by torchrun (one process per GPU, NCCL).  Rank r owns E/G experts
+(contiguous ids, or the balanced placement with --placement balanced) and
+T/G of the tokens; one step = ExpertParallelW13.forward (permute, count
+exchange, bf16 dispatch all_to_all, local permute + FP8 quant + grouped GEMM,
+combine all_to_all).  Strong scaling: the global batch is fixed as G grows.
+Timing: CUDA events per step on each rank's stream, 256 MB L2 flush between
+steps, barrier + synchronize around the timed region, max over ranks.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+FLUSH_BYTES = 256 << 20
+
+
+def _max(x: float, dev) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum(x: float, dev) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def run(args, cfg):
+    import bench  # contract helpers (peaks, clocks, algorithmic bytes)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    try:
+        from . import build
+        if local == 0:
+            build.build()
+        dist.barrier()
+        from . import data
+        from .ep import ExpertParallelW13, StepTimers, balanced_placement
+
+        G = world
+        if cfg.E % G or cfg.T % G:
+            raise ValueError(f"E={cfg.E} and T={cfg.T} must divide by {G}")
+        El, Tl = cfg.E // G, cfg.T // G
+        ids_g = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s)
+        hidden_g = data.activations(cfg.T, cfg.K)
+        placement = None
+        if getattr(args, "placement", "contiguous") == "balanced":
+            placement = balanced_placement(torch.bincount(ids_g.reshape(-1), minlength=cfg.E), G)
+        table = placement if placement is not None else torch.arange(cfg.E, dtype=torch.int32)
+        mine = table[rank * El:(rank + 1) * El]
+        W, Ws = data.fp8_weights(El, cfg.N, cfg.K, seed=1000 + rank, device=dev)
+        ids = ids_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
+        hidden = hidden_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
+        ep = ExpertParallelW13(W, Ws, cfg.E, silu=cfg.silu, placement=placement)
+
+        flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream()
+        for _ in range(args.warmup):
+            ep.forward(hidden, ids)
+        torch.cuda.synchronize()
+        dist.barrier()
+
+        K = args.steps
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(K)]
+        tm = [StepTimers(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(K)]
+        clocks = bench.Clocks(local) if rank == 0 else None
+        torch.cuda.synchronize()
+        dist.barrier()
+        if clocks:
+            clocks.start()
+        for i in range(K):
+            flush.zero_()
+            ev[i][0].record(stream)
+            out = ep.forward(hidden, ids, timers=tm[i])
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        clk = clocks.stop() if clocks else None
+        step_ms = sum(a.elapsed_time(b) for a, b in ev) / K
+        gemm_ms = sum(t.gemm_start.elapsed_time(t.gemm_end) for t in tm) / K
+
+        # e2e: host buffers in, host buffer out, through the same public API
+        h_hidden = hidden.cpu().pin_memory()
+        h_ids = ids.cpu().pin_memory()
+        h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        d_hidden, d_ids = torch.empty_like(hidden), torch.empty_like(ids)
+        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(K)]
+        dist.barrier()
+        for i in range(K):
+            flush.zero_()
+            ev2[i][0].record(stream)
+            d_hidden.copy_(h_hidden, non_blocking=True)
+            d_ids.copy_(h_ids, non_blocking=True)
+            o = ep.forward(d_hidden, d_ids)
+            h_out.copy_(o, non_blocking=True)
+            ev2[i][1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = sum(a.elapsed_time(b) for a, b in ev2) / K
+
+        # local GEMM algorithmic bytes (this rank's experts and received rows)
+        flat = ids_g.reshape(-1)
+        owner_slot = torch.empty(cfg.E, dtype=torch.int64)
+        owner_slot[table.long()] = torch.arange(cfg.E)
+        loc_counts = torch.bincount(owner_slot[flat.long()], minlength=cfg.E)[rank * El:(rank + 1) * El]
+        byts, _, active = bench.fp8_algorithmic(cfg, loc_counts.tolist())
+        R_global = int(flat.numel())
+        flops = 2.0 * R_global * cfg.N * cfg.K
+
+        max_step = _max(step_ms, dev)
+        max_gemm = _max(gemm_ms, dev)
+        max_e2e = _max(e2e_ms, dev)
+        gemm_bw = byts / (gemm_ms * 1e-3) / 1e9
+        min_bw = -_max(-gemm_bw, dev)
+        sum_active = _sum(float(active), dev)
+        max_rows = _max(float(loc_counts.sum()), dev)
+        if rank != 0:
+            return None
+        pk = bench.peaks()
+        return {
+            "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
+            "value": round(flops / (max_step * 1e-3) / 1e12, 3),
+            "unit": "TFLOPS",
+            "n_gpus": G,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": round(max_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out; bf16 dispatch",
+            "data": "synthetic (seeded), random-init weights",
+            "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
+                       "routed_rows": R_global, "K": cfg.K, "N": cfg.N, "silu": cfg.silu,
+                       "routing": cfg.routing,
+                       "parallelism": f"ep{G} ({El} experts and {Tl} tokens per GPU, "
+                                      f"{'balanced' if placement is not None else 'contiguous'} placement)",
+                       "active_experts_total": int(sum_active), "max_rows_per_gpu": int(max_rows),
+                       "l2": "256 MB flush between timed steps"},
+            "roofline": {"bound": "hbm", "kernel": "fp8_w13_grouped_kernel (per-GPU local GEMM, slowest rank)",
+                         "achieved": round(min_bw, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(min_bw / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                         "kernel_ms": round(max_gemm, 4), "traffic": None},
+            "e2e": {"value": round(flops / (max_e2e * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+                    "ms_per_step": round(max_e2e, 4),
+                    "h2d_bytes_per_step": (h_hidden.numel() * 2 + h_ids.numel() * 4) * G,
+                    "d2h_bytes_per_step": h_out.numel() * 2 * G},
+            "gpu_launches": 4 * K,
+            "clocks": clk,
+        }
+    finally:
+        dist.destroy_process_group()

@@ -1,0 +1,124 @@
+"""Expert-parallel host logic on CPU ranks (gloo, world size 2 and 4).
+
+The distributed orchestration in ferret_b200/ep.py (count exchange, split
+sizes, dispatch/combine all_to_all, the per-rank re-permutation and the final
+scatter) runs unchanged; the three device kernels are replaced by the CPU
+oracle (test infrastructure) through the ``kernels`` hook.  Every (token, slot)
+output must equal the single-process result bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+
+class OracleKernels:
+    """CPU stand-ins for the CUDA kernels, built on the oracle."""
+
+    def permute(self, ids, E):
+        rows, offs, _ = O.moe_permute(ids.numpy(), E)
+        return torch.from_numpy(rows), torch.from_numpy(offs)
+
+    def quant(self, x, rows, div):
+        q, s = O.quant_act_fp8_1x128(x.view(torch.int16).numpy().view(np.uint16), rows.numpy(), div)
+        return torch.from_numpy(q), torch.from_numpy(s)
+
+    def gemm(self, q, s, W, Ws, offsets, silu):
+        offs = offsets.numpy()
+        mi = np.repeat(np.arange(len(offs) - 1), np.diff(offs)).astype(np.int32)
+        mi = np.concatenate([mi, -np.ones(q.shape[0] - len(mi), np.int32)])
+        out = O.fp8_grouped_gemm(q.numpy(), s.numpy(), W.view(torch.uint8).numpy(), Ws.numpy(), mi,
+                                 silu=silu)
+        return torch.from_numpy(O.f32_to_bf16(np.nan_to_num(out)).view(np.int16)).view(torch.bfloat16)
+
+
+E, N, K, T, TOPK = 8, 256, 256, 24, 3
+
+
+def make_global(seed=0):
+    from ferret_b200 import data
+    W, Ws = data.fp8_weights(E, N, K, seed=seed + 1)
+    hidden = data.activations(T, K, seed=seed + 2)
+    ids = data.routing(T, E, TOPK, "zipf", seed=seed + 3)
+    ids[0, 0] = -1                                     # an invalid id is dropped
+    return W, Ws, hidden, ids
+
+
+def reference(silu):
+    W, Ws, hidden, ids = make_global()
+    from ferret_b200.ep import ExpertParallelW13
+    ep = ExpertParallelW13(W, Ws, E, silu=silu, kernels=OracleKernels())
+    return ep.forward(hidden, ids)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, silu, balanced, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from ferret_b200.ep import ExpertParallelW13, balanced_placement
+        W, Ws, hidden, ids = make_global()
+        placement = None
+        if balanced:
+            flat = ids.reshape(-1)
+            placement = balanced_placement(torch.bincount(flat[flat >= 0], minlength=E), world)
+        table = placement if placement is not None else torch.arange(E)
+        El = E // world
+        mine = table[rank * El:(rank + 1) * El].long()
+        t0, t1 = rank * T // world, (rank + 1) * T // world
+        ep = ExpertParallelW13(W[mine], Ws[mine], E, silu=silu, placement=placement,
+                               kernels=OracleKernels())
+        out = ep.forward(hidden[t0:t1], ids[t0:t1])
+        outs = [torch.empty((T // world) * TOPK, out.shape[1] * 2, dtype=torch.uint8)
+                for _ in range(world)]
+        dist.all_gather(outs, out.view(torch.uint8))
+        if rank == 0:
+            q.put(torch.cat(outs).view(torch.int16).numpy())
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,silu,balanced", [(2, False, False), (2, True, True), (4, False, True)])
+def test_ep_matches_single_process(world, silu, balanced):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, silu, balanced, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=240)
+    assert not isinstance(got, str), got
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = reference(silu).view(torch.int16).numpy()
+    assert got.shape == ref.shape
+    assert np.array_equal(got, ref)
+    assert not ref[0].any()          # the dropped pair is a zero row
+
+
+def test_balanced_placement_evens_load():
+    from ferret_b200.ep import balanced_placement
+    counts = torch.tensor([100, 1, 1, 1, 50, 50, 2, 2])
+    table = balanced_placement(counts, 2)
+    assert sorted(table.tolist()) == list(range(8))
+    loads = [int(counts[table[:4].long()].sum()), int(counts[table[4:].long()].sum())]
+    assert max(loads) - min(loads) <= 50

@@ -254,3 +254,25 @@ def test_w13_path_dsv3_decode_full_size(ops):
         err = O.rel_err(got[r0:r1], ref)
         assert err["nan"] == 0 and err["max_rel"] < TOL, (int(e), err)
     assert ops.last_device_status() == 0
+
+
+# ---------------------------------------------------------------- expert parallel, one rank
+
+def test_ep_single_rank_matches_w13_path(ops):
+    """ExpertParallelW13 with one rank (no communication) against fp8_moe_w13:
+    bit-identical per (token, slot) pair."""
+    from ferret_b200 import data
+    from ferret_b200.ep import ExpertParallelW13
+    cfg = data.CONFIGS["cpu_fp8"]
+    dev = torch.device("cuda")
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K).to(dev)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, "zipf").to(dev)
+    for silu in (False, True):
+        out, rows, offs = ops.fp8_moe_w13(hidden, ids, W, Ws, silu=silu)
+        tk = torch.empty_like(out)
+        tk[rows.long()] = out
+        ep = ExpertParallelW13(W, Ws, cfg.E, silu=silu)
+        got = ep.forward(hidden, ids)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), tk.view(torch.int16))
