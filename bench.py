@@ -123,6 +123,17 @@ def fp8_algorithmic(cfg, counts):
     return byts, flops, active
 
 
+def int4_algorithmic(cfg, counts):
+    """SURVEY-defined algorithmic bytes and FLOPs for the INT4 W13 GEMM, and the
+    reference's narrower INT4 weight bytes (baseline_marlin.py:204-206)."""
+    R = int(sum(counts))
+    active = sum(1 for c in counts if c > 0)
+    n_out = cfg.N // 2 if cfg.silu else cfg.N
+    wbytes = active * (cfg.N * cfg.K // 2)
+    byts = wbytes + active * cfg.N * (cfg.K // 32) * 2 + cfg.T * cfg.K * 2 + R * n_out * 2
+    return byts, 2.0 * R * cfg.N * cfg.K, active, wbytes
+
+
 def read_traffic(kernel_tag):
     """dram bytes per launch recorded from an ncu capture in profiles/<tag>.md."""
     path = os.path.join(ROOT, "profiles", f"{kernel_tag}.md")
@@ -176,6 +187,8 @@ def run_single(args, cfg):
     import torch
     from ferret_b200 import build, data, ops
     build.build()
+    if cfg.quant == "int4":
+        return run_single_int4(args, cfg)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     W, W_s = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
@@ -289,6 +302,100 @@ def run_single(args, cfg):
     if not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(bufs.a.cpu(), bufs.a_scale.cpu(), W, W_s, offsets, cfg)
     return res
+
+
+def run_single_int4(args, cfg):
+    """Kimi-style INT4 W4A16 W13 on one GPU: permute + INT4 grouped GEMM."""
+    import torch
+    from ferret_b200 import data, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    raw, scales = data.int4_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    packed = ops.int4_repack_w13(raw)
+    del raw
+    hidden = data.activations(cfg.T, cfg.K).to(dev)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
+    n_out = cfg.N // 2 if cfg.silu else cfg.N
+    out = torch.zeros(cfg.R, n_out, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out)
+
+    if args.gemm_only:
+        perm = ops.moe_permute(ids, cfg.E)
+        for _ in range(args.gemm_only):
+            ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out, perm=perm)
+        torch.cuda.synchronize()
+        return None
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def timed(fn, k):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(k)]
+        for i in range(k):
+            flush.zero_()
+            evs[i][0].record(stream)
+            fn()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
+
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    step_ms = timed(step, args.steps)
+    clk = clocks.stop()
+    perm = ops.moe_permute(ids, cfg.E)
+    gemm_ms = timed(lambda: ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out,
+                                              perm=perm), args.steps)
+    h_hidden, h_ids = hidden.cpu().pin_memory(), ids.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_hidden, d_ids = torch.empty_like(hidden), torch.empty_like(ids)
+
+    def e2e():
+        d_hidden.copy_(h_hidden, non_blocking=True)
+        d_ids.copy_(h_ids, non_blocking=True)
+        ops.moe_wna16_w13(d_hidden, packed, scales, d_ids, silu=cfg.silu, out=out)
+        h_out.copy_(out, non_blocking=True)
+    e2e_ms = timed(e2e, args.steps)
+    if ops.last_device_status() != 0:
+        raise RuntimeError("device status error after timing")
+    counts = torch.bincount(ids.reshape(-1).cpu().long(), minlength=cfg.E).tolist()
+    byts, flops, active, wbytes = int4_algorithmic(cfg, counts)
+    ms = sum(step_ms) / len(step_ms)
+    g_ms = sum(gemm_ms) / len(gemm_ms)
+    e_ms = sum(e2e_ms) / len(e2e_ms)
+    pk = peaks()
+    achieved = byts / (g_ms * 1e-3) / 1e9
+    return {
+        "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
+        "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights dequantized to bf16 x bf16 -> f32 accumulate, bf16 out",
+        "data": "synthetic (seeded), random-init weights",
+        "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
+                   "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
+                   "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
+                   "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
+        "int4_weight_tbs": round(wbytes / (g_ms * 1e-3) / 1e12, 3),
+        "roofline": {"bound": "hbm", "kernel": "int4_w13_grouped_kernel",
+                     "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "peak_source": pk["source"] + " (hbm_gbs)", "algorithmic_bytes": byts,
+                     "kernel_ms": round(g_ms, 4),
+                     "kernel_tflops": round(flops / (g_ms * 1e-3) / 1e12, 3),
+                     "traffic": read_traffic(f"int4_w13_grouped_{cfg.name}")},
+        "e2e": {"value": round(flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+                "ms_per_step": round(e_ms, 4),
+                "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
+                "d2h_bytes_per_step": h_out.numel() * 2},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
 
 
 # ---------------------------------------------------------------------------

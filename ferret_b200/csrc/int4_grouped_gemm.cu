@@ -1,0 +1,519 @@
+// int4_grouped_gemm.cu -- W4A16 (INT4 group-32 symmetric weights, bf16
+// activations) grouped GEMM for the MoE W13 projection on sm_100a, the
+// operation of vLLM's moe_wna16_marlin_gemm + apply_moe_activation(SILU) as
+// the reference times it (baselines/kimi-moe-w13-int4/baseline_marlin.py:140-168).
+//
+//   w[e, n, k]   = bf16((nibble(e, k, n) - 8) * scale[e, k/32, n])
+//   out[p, n]    = sum_k hidden[p / topk, k] * w[e(p), n, k]            (bf16)
+//   SiLU variant = silu(out[p, j]) * out[p, N/2 + j]  for j < N/2
+// with p the flat (token, slot) index; rows are written in that (token, slot)
+// order, as Marlin writes them.
+//
+// tcgen05 has no INT4 operand type, so the weights are dequantized on chip:
+//   * warp 0 (TMA): per 128-wide K block, the packed weight box (128 n x 16
+//     int32 = 8 KB), its bf16 scales (128 n x 4 groups = 1 KB) and, one
+//     128-byte box per token row, the activation rows of the tile straight
+//     from `hidden` (no gather pass) into an NS-deep ring;
+//   * warps 2-9 (dequant, 256 threads): each thread turns 4 packed words of
+//     one weight row (32 K values, one scale) into four 16-byte bf16 chunks,
+//     written into the 128-byte-swizzled K-major layout the MMA reads, in a
+//     second, shallower ring;
+//   * warp 1 (MMA): tcgen05.mma.kind::f16 (bf16 x bf16 -> f32), M = 128 weight
+//     rows, N = NT token rows (swap-AB), K = 16, accumulating the whole K
+//     range in one TMEM buffer per tile (double-buffered across tiles);
+//   * warps 10-13 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
+// The dequant arithmetic is exact: nibble pairs become bf16 (128 + n) with one
+// lop3 against the 0x4300 exponent, minus 136 gives n - 8 exactly, and one
+// bf16x2 multiply by the scale rounds once -- the oracle's bf16((n-8)*s).
+// For that the nibbles of each word are pre-permuted once at load time
+// (ferret_int4_repack_w13) so that the pairs (k, k+1) sit 16 bits apart.
+#include <algorithm>
+
+#include "capi_internal.h"
+
+namespace ferret {
+namespace {
+
+constexpr int kI4Threads = 448;      // 14 warps
+constexpr int kDqWarp0 = 2, kDqWarps = 8, kDqThreads = kDqWarps * 32;
+constexpr int kEpiWarp0 = 10, kI4EpiThreads = 128;
+constexpr int kI4MaxE = 1024;
+constexpr int kI4MaxStages = 16, kI4MaxDq = 4, kI4MaxAcc = 4;
+constexpr int kRawW = 128 * 16 * 4;    // packed box: 128 n x 16 words
+constexpr int kRawS = 128 * 4 * 2;     // scales: 128 n x 4 groups bf16
+constexpr int kDqTile = 128 * 128 * 2; // bf16 128 n x 128 k (two 64-wide atoms)
+
+enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_DQE = 3, I4_DQF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7 };
+
+struct Int4Args {
+    const int32_t* sorted_rows;   // flat (token, slot) of each expert-sorted row
+    const int32_t* offsets;       // [E+1]
+    __nv_bfloat16* out;
+    int T, topk, N, K, E, R;
+    int stages, dq_stages;
+    DevCtl ctl;
+};
+
+template <int NT, bool PAIR>
+struct I4Cfg {
+    static constexpr int kW = PAIR ? 2 : 1;
+    static constexpr int kBTile = NT * 256;                     // NT rows x 128 k bf16
+    static constexpr int kStage = kW * (kRawW + kRawS) + kBTile;
+    static constexpr int kCols = NT * kW;
+    static constexpr int kAcc = 2;
+    static constexpr int kUsed = kAcc * kCols;
+    static constexpr int kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : 256;
+};
+
+struct I4Layout {
+    int raw_off, dq_off, mts_off, part_off, bar_off, misc_off, total;
+};
+
+__host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int dq_bytes,
+                                              int dq_stages, int E) {
+    I4Layout L;
+    int o = 0;
+    L.dq_off = o;                            // 1024-aligned swizzled tiles first
+    o += dq_bytes * dq_stages;
+    L.raw_off = o;                           // B tiles inside need 1024 alignment
+    o += stage_bytes * stages;
+    L.mts_off = o;
+    o += 4 * (E + 1);
+    L.part_off = o;
+    o += 4 * (kI4Threads + 1);
+    o = (o + 7) & ~7;
+    L.bar_off = o;
+    o += 8 * (2 * kI4MaxStages + 2 * kI4MaxDq + 2 * kI4MaxAcc + 1);
+    L.misc_off = o;
+    o += 16;
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// One repacked word (slots hold k offsets 0,2,4,6,1,3,5,7) and the scale
+// pair (s, s) -> 8 bf16 weights for k offsets 0..7, as four bf16x2 words.
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2) {
+    const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u, kBias = 0x43084308u;  // 128, 136
+    uint4 r;
+    r.x = bf16x2_mul(bf16x2_sub(lop3_and_or(w, kMask, kMagic), kBias), s2);
+    r.y = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 4, kMask, kMagic), kBias), s2);
+    r.z = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 8, kMask, kMagic), kBias), s2);
+    r.w = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 12, kMask, kMagic), kBias), s2);
+    return r;
+}
+
+template <int NT>
+__device__ __forceinline__ void i4_decode_tile(int t, int nbc, int E, const int* mt_start,
+                                               const int32_t* offs, int& e, int& row0, int& rows,
+                                               int& nb) {
+    const int mt = t / nbc;
+    nb = t - mt * nbc;
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (mt_start[mid] <= mt) lo = mid;
+        else hi = mid - 1;
+    }
+    e = lo;
+    const int local = (mt - mt_start[e]) * NT;
+    row0 = __ldg(offs + e) + local;
+    rows = min(NT, __ldg(offs + e + 1) - row0);
+}
+
+template <int NT, bool PAIR>
+__global__ void __launch_bounds__(kI4Threads, 1)
+    int4_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_w,
+                            const __grid_constant__ CUtensorMap tm_s,
+                            const __grid_constant__ CUtensorMap tm_x, const Int4Args args) {
+    using C = I4Cfg<NT, PAIR>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int N = args.N, K = args.K, E = args.E, NS = args.stages, ND = args.dq_stages;
+    const int nk = K >> 7;
+    const int nbc = PAIR ? (N >> 8) : (N >> 7);
+    const int kq = K >> 3, kg = K >> 5;     // packed rows / scale rows per expert
+    const I4Layout L = i4_layout(C::kStage, NS, C::kW * kDqTile, ND, E);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kI4MaxStages + s); };
+    auto dqf_bar = [&](int d) { return bar0 + 8u * (2 * kI4MaxStages + d); };
+    auto dqe_bar = [&](int d) { return bar0 + 8u * (2 * kI4MaxStages + kI4MaxDq + d); };
+    auto tf_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + a); };
+    auto te_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + kI4MaxAcc + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + 2 * kI4MaxAcc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    uint8_t* raw = smem + L.raw_off;
+    uint8_t* dq = smem + L.dq_off;
+    const uint32_t raw_base = smem_addr(raw), dq_base = smem_addr(dq);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int d = 0; d < ND; ++d) {
+            mbar_init(dqf_bar(d), kDqWarps);
+            mbar_init(dqe_bar(d), 1);
+        }
+        for (int a = 0; a < C::kAcc; ++a) {
+            mbar_init(tf_bar(a), 1);
+            mbar_init(te_bar(a), kI4EpiThreads);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kI4Threads) {
+        const int s = args.offsets[e], c = args.offsets[e + 1] - s;
+        if (s < 0 || c < 0 || s + c > args.R) seg_bad = true;
+        mt_start[e] = (s < 0 || c < 0 || s + c > args.R) ? 0 : (c + NT - 1) / NT;
+    }
+    if (seg_bad) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_s);
+            tma_prefetch_desc(&tm_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
+                int tok[NT];
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+                    tok[j] = j < rows ? __ldg(args.sorted_rows + row0 + j) / args.topk : 0;
+                const int ncol = nb * 128, ncol_up = (N >> 1) + nb * 128;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % NS;
+                    if (!mbar_wait(empty_bar(s), ((it / NS) & 1) ^ 1, abort_flag, args.ctl, I4_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = raw_base + s * C::kStage;
+                    mbar_expect_tx(full_bar(s), C::kW * (kRawW + kRawS) + rows * 256);
+                    tma_load_2d_hint(st, &tm_w, ncol, e * kq + kb * 16, full_bar(s), pol_w);
+                    tma_load_2d_hint(st + C::kW * kRawW, &tm_s, ncol, e * kg + kb * 4, full_bar(s), pol_w);
+                    if (PAIR) {
+                        tma_load_2d_hint(st + kRawW, &tm_w, ncol_up, e * kq + kb * 16, full_bar(s), pol_w);
+                        tma_load_2d_hint(st + C::kW * kRawW + kRawS, &tm_s, ncol_up, e * kg + kb * 4,
+                                         full_bar(s), pol_w);
+                    }
+                    const uint32_t bt = st + C::kW * (kRawW + kRawS);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        if (j < rows) {
+                            tma_load_2d_hint(bt + j * 128, &tm_x, kb * 128, tok[j], full_bar(s), pol_x);
+                            tma_load_2d_hint(bt + NT * 128 + j * 128, &tm_x, kb * 128 + 64, tok[j],
+                                             full_bar(s), pol_x);
+                        }
+                    }
+                }
+            }
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, I4_DRAIN, false);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (elect_one()) {
+            constexpr uint32_t idesc = make_idesc(128, NT, 1, 1);
+            int it = 0, tcount = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tcount) {
+                const int a = tcount % C::kAcc;
+                if (!mbar_wait(te_bar(a), ((tcount / C::kAcc) & 1) ^ 1, abort_flag, args.ctl, I4_TE))
+                    break;
+                const uint32_t d_acc = tmem_base + a * C::kCols;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % NS, d = it % ND;
+                    // the B tile comes straight from TMA; the dequantized A tile
+                    // from the dequant warps
+                    if (!mbar_wait(full_bar(s), (it / NS) & 1, abort_flag, args.ctl, I4_FULL) ||
+                        !mbar_wait(dqf_bar(d), (it / ND) & 1, abort_flag, args.ctl, I4_DQF)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t bt = raw_base + s * C::kStage + C::kW * (kRawW + kRawS);
+                    const uint32_t wt = dq_base + d * (C::kW * kDqTile);
+#pragma unroll
+                    for (int ac = 0; ac < 2; ++ac) {
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint32_t acc = (kb | ac | ks) ? 1u : 0u;
+                            const uint64_t bdesc = sdesc_k_sw128(bt + ac * NT * 128 + ks * 32);
+                            mma_f16(d_acc, sdesc_k_sw128(wt + ac * 16384 + ks * 32), bdesc, idesc, acc);
+                            if (PAIR)
+                                mma_f16(d_acc + NT, sdesc_k_sw128(wt + kDqTile + ac * 16384 + ks * 32),
+                                        bdesc, idesc, acc);
+                        }
+                    }
+                    tc_commit(empty_bar(s));
+                    tc_commit(dqe_bar(d));
+                }
+                if (!ok) break;
+                tc_commit(tf_bar(a));
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, I4_DRAIN, false);
+        }
+    } else if (warp < kEpiWarp0) {
+        // ================= dequant =================
+        const int dt = tid - kDqWarp0 * 32;     // 0..255
+        const int n = dt & 127, g0 = dt >> 7;   // groups g0 and g0 + 2
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int s = it % NS, d = it % ND;
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(full_bar(s), (it / NS) & 1, abort_flag, args.ctl, I4_FULL) &&
+                                    mbar_wait(dqe_bar(d), ((it / ND) & 1) ^ 1, abort_flag, args.ctl, I4_DQE));
+                if (!ok) break;
+                const uint8_t* st = raw + s * C::kStage;
+                uint8_t* out_tile = dq + d * (C::kW * kDqTile);
+#pragma unroll
+                for (int w = 0; w < C::kW; ++w) {
+                    const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kRawW);
+                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + C::kW * kRawW + w * kRawS);
+                    uint8_t* tile = out_tile + w * kDqTile;
+#pragma unroll
+                    for (int gi = 0; gi < 2; ++gi) {
+                        const int g = g0 + 2 * gi;
+                        const uint32_t s1 = sc[g * 128 + n];
+                        const uint32_t s2 = s1 | (s1 << 16);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int k8 = g * 4 + q;                    // 0..15
+                            const uint4 v = dequant_word(words[k8 * 128 + n], s2);
+                            const int ac = k8 >> 3, c = k8 & 7;
+                            *reinterpret_cast<uint4*>(tile + ac * 16384 + n * 128 + ((c ^ (n & 7)) << 4)) = v;
+                        }
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(dqf_bar(d));
+            }
+        }
+    } else {
+        // ================= epilogue =================
+        const int q = warp & 3;
+        const int ldo = PAIR ? (N >> 1) : N;
+        int tcount = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ++tcount) {
+            int e, row0, rows, nb;
+            i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
+            const int a = tcount % C::kAcc;
+            if (!__all_sync(0xffffffffu, mbar_wait(tf_bar(a), (tcount / C::kAcc) & 1, abort_flag,
+                                                   args.ctl, I4_TF)))
+                break;
+            tc_fence_after();
+            const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * C::kCols;
+            float g[NT], u[PAIR ? NT : 1];
+#pragma unroll
+            for (int c = 0; c < NT; c += 8) {
+                uint32_t r[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                               "=r"(r[6]), "=r"(r[7])
+                             : "r"(tb + c));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) g[c + j] = __uint_as_float(r[j]);
+                if (PAIR) {
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+                                   "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                                 : "r"(tb + NT + c));
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) u[PAIR ? c + j : 0] = __uint_as_float(r[j]);
+                }
+            }
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(te_bar(a));
+            const int ncol = nb * 128 + q * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                if (j < rows) {
+                    const int orow = __ldg(args.sorted_rows + row0 + j);
+                    const float v = PAIR ? silu_mul(g[j], u[PAIR ? j : 0]) : g[j];
+                    args.out[(size_t)orow * ldo + ncol] = __float2bfloat16_rn(v);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// Load-time nibble permutation: slot i of each word receives K offset
+// perm[i] = {0,2,4,6,1,3,5,7}[i], so (k, k+1) pairs are 16 bits apart.
+__global__ void int4_repack_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
+                                   size_t words) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t w = in[i];
+        uint32_t r = 0;
+#pragma unroll
+        for (int slot = 0; slot < 8; ++slot) {
+            const int k = slot < 4 ? 2 * slot : 2 * (slot - 4) + 1;
+            r |= ((w >> (4 * k)) & 0xFu) << (4 * slot);
+        }
+        out[i] = r;
+    }
+}
+
+template <int NT, bool PAIR>
+int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_packed,
+                const void* scales, const int32_t* sorted_rows, const int32_t* offsets, void* out,
+                int T, int topk, int N, int K, int E, int R, cudaStream_t stream) {
+    using C = I4Cfg<NT, PAIR>;
+    CUtensorMap tm_w, tm_s, tm_x;
+    int rc = make_tmap_2d(&tm_w, w_packed, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, (uint64_t)E * (K / 8), N,
+                          (uint64_t)N * 4, 128, 16, false);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_s, scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E * (K / 32), N,
+                      (uint64_t)N * 2, 128, 4, false);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_x, hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K, (uint64_t)K * 2, 64, 1,
+                      true);
+    if (rc != FERRET_OK) return rc;
+    const int budget = info->max_smem_optin - 1024;
+    const int dq_bytes = C::kW * kDqTile;
+    const int nd = PAIR ? 2 : 3;
+    const I4Layout l0 = i4_layout(C::kStage, 0, dq_bytes, nd, E);
+    const int stages = std::min(kI4MaxStages, (budget - l0.total) / C::kStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const I4Layout L = i4_layout(C::kStage, stages, dq_bytes, nd, E);
+    const int smem = L.total + 1024;
+    auto kern = int4_w13_grouped_kernel<NT, PAIR>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    Int4Args a;
+    a.sorted_rows = sorted_rows;
+    a.offsets = offsets;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.T = T;
+    a.topk = topk;
+    a.N = N;
+    a.K = K;
+    a.E = E;
+    a.R = R;
+    a.stages = stages;
+    a.dq_stages = nd;
+    a.ctl = make_ctl(info);
+    kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_w, tm_s, tm_x, a);
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace ferret
+
+using namespace ferret;
+
+extern "C" int ferret_int4_repack_w13(const int32_t* w_raw, int32_t* w_packed, int E, int K, int N,
+                                      void* stream) {
+    if (E <= 0 || K <= 0 || N <= 0 || K % 8) return FERRET_ERR_SHAPE;
+    if (!w_raw || !w_packed) return FERRET_ERR_NULL;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    const size_t words = (size_t)E * (K / 8) * N;
+    const int grid = (int)std::min<size_t>((words + 255) / 256, (size_t)info->num_sms * 16);
+    int4_repack_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const uint32_t*>(w_raw), reinterpret_cast<uint32_t*>(w_packed), words);
+    return launch_status();
+}
+
+extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const int32_t* w_packed,
+                                   const void* w_scale_bf16, const int32_t* sorted_rows,
+                                   const int32_t* expert_offsets, void* out_bf16, int T, int topk,
+                                   int N, int K, int E, int flags, void* stream) {
+    const bool pair = (flags & FERRET_SILU_MUL) != 0;
+    if (T < 0 || topk <= 0 || N <= 0 || K <= 0 || E <= 0 || E > kI4MaxE) return FERRET_ERR_SHAPE;
+    if (K % 128 || N % 128 || (pair && N % 256)) return FERRET_ERR_SHAPE;
+    if ((long long)E * (K / 8) >= (1ll << 31) || (long long)T * topk >= (1ll << 31))
+        return FERRET_ERR_SHAPE;
+    if (T == 0) return FERRET_OK;
+    if (!hidden_bf16 || !w_packed || !w_scale_bf16 || !sorted_rows || !expert_offsets || !out_bf16)
+        return FERRET_ERR_NULL;
+    if (!aligned16(hidden_bf16) || !aligned16(w_packed) || !aligned16(w_scale_bf16) ||
+        (reinterpret_cast<uintptr_t>(out_bf16) & 1u))
+        return FERRET_ERR_ALIGN;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    cudaStream_t s = as_stream(stream);
+    const int R = T * topk;
+    int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
+    if (nt == 0) {
+        const int avg = (R + E - 1) / E;
+        nt = avg <= 4 ? 8 : avg <= 12 ? 16 : 32;
+    }
+    switch (nt) {
+        case 8:
+            return pair ? launch_int4<8, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                               expert_offsets, out_bf16, T, topk, N, K, E, R, s)
+                        : launch_int4<8, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s);
+        case 16:
+            return pair ? launch_int4<16, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s)
+                        : launch_int4<16, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                                 expert_offsets, out_bf16, T, topk, N, K, E, R, s);
+        case 32:
+            return pair ? launch_int4<32, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s)
+                        : launch_int4<32, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
+                                                 expert_offsets, out_bf16, T, topk, N, K, E, R, s);
+        default:
+            return FERRET_ERR_SHAPE;
+    }
+}

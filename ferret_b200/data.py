@@ -45,6 +45,13 @@ CONFIGS = {
                                    routing="zipf", silu=True),
     "kimi_int4_decode": W13Config("kimi_int4_decode", E=384, topk=8, T=64, K=7168, N=4096,
                                   quant="int4"),
+    "kimi_int4_decode_silu": W13Config("kimi_int4_decode_silu", E=384, topk=8, T=64, K=7168,
+                                       N=4096, quant="int4", silu=True),
+    # the reference's own Kimi TP8 shape (2I_r = 512, T in {1, 8}), fused SiLU
+    "kimi_int4_tp8_t1": W13Config("kimi_int4_tp8_t1", E=384, topk=8, T=1, K=7168, N=512,
+                                  quant="int4", silu=True),
+    "kimi_int4_tp8_t8": W13Config("kimi_int4_tp8_t8", E=384, topk=8, T=8, K=7168, N=512,
+                                  quant="int4", silu=True),
     "ep_prefill": W13Config("ep_prefill", E=256, topk=8, T=32768, K=7168, N=4096, routing="zipf"),
     # one EP=8 rank of the decode config (32 local experts, ~4 rows each): the
     # reference's own per-rank decode shape (tasks/fp8-group-gemm-dsv3-decode.yaml:14),
