@@ -28,6 +28,7 @@ SIGNATURES = {
     "ferret_strerror": (ctypes.c_char_p, [_i]),
     "ferret_set_wait_timeout_ns": (_i, [ctypes.c_ulonglong]),
     "ferret_last_device_status": (_i, [_p, ctypes.POINTER(ctypes.c_int32)]),
+    "ferret_selftest_wait_timeout": (_i, [ctypes.c_ulonglong, _p]),
     "ferret_moe_permute": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "ferret_quant_act_fp8_1x128": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous": (

@@ -145,3 +145,39 @@ extern "C" int ferret_last_device_status(void* stream, int32_t* status) {
     *status = host;
     return FERRET_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded-wait machinery: one CTA waits on an mbarrier that
+// nothing ever arrives on.  The wait must give up after `timeout_ns`, record
+// DEV_TIMEOUT (site 15) in the status word and let the kernel return -- the
+// same path every pipeline wait takes when a peer role stops making progress.
+// ---------------------------------------------------------------------------
+namespace ferret {
+namespace {
+
+__global__ void wait_timeout_selftest_kernel(DevCtl ctl) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(&bar), 1);
+        abort_flag = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(smem_addr(&bar), 0, &abort_flag, ctl, 15);
+    __syncthreads();
+}
+
+}  // namespace
+}  // namespace ferret
+
+extern "C" int ferret_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
+    if (timeout_ns == 0 || timeout_ns > 10000000000ull) return FERRET_ERR_SHAPE;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    DevCtl c = make_ctl(info);
+    c.timeout_ns = timeout_ns;
+    wait_timeout_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>(c);
+    return launch_status();
+}

@@ -88,6 +88,21 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes or `hint_ns` passes, instead of spinning and
+// taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 //   abort_flag: CTA-wide flag in shared memory; when `respect_abort` is true
 //               the wait gives up as soon as another role raised it.
@@ -96,15 +111,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           const DevCtl& ctl, int site, bool respect_abort = true) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_test(bar, parity)) return true;
-        if ((it & 31u) == 0) {
-            if (respect_abort && *abort_flag) return false;
-            if (global_ns() - t0 > ctl.timeout_ns) {
-                *abort_flag = 1;
-                report(ctl, DEV_TIMEOUT | (site << 8));
-                return false;
-            }
+    for (;;) {
+        // sleep up to 0.5 ms per try; completion wakes the thread early
+        if (mbar_test_sleep(bar, parity, 500000u)) return true;
+        if (respect_abort && *abort_flag) return false;
+        if (global_ns() - t0 > ctl.timeout_ns) {
+            *abort_flag = 1;
+            report(ctl, DEV_TIMEOUT | (site << 8));
+            return false;
         }
     }
 }

@@ -425,7 +425,7 @@ int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_pac
     if (rc != FERRET_OK) return rc;
     const int budget = info->max_smem_optin - 1024;
     const int dq_bytes = C::kW * kDqTile;
-    const int nd = PAIR ? 2 : 3;
+    const int nd = PAIR ? 2 : 4;
     const I4Layout l0 = i4_layout(C::kStage, 0, dq_bytes, nd, E);
     const int stages = std::min(kI4MaxStages, (budget - l0.total) / C::kStage);
     if (stages < 2) return FERRET_ERR_SHAPE;

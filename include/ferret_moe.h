@@ -66,6 +66,12 @@ FERRET_API int ferret_set_wait_timeout_ns(unsigned long long ns);
  * expert rows, 4 gather index out of range. */
 FERRET_API int ferret_last_device_status(void* stream, int32_t* status);
 
+/* Self-test of the device-side failure detection: launches one CTA whose
+ * only wait can never complete; the wait gives up after timeout_ns (at most
+ * 10 s), records status 1 | (15 << 8) and the kernel returns.  No counterpart
+ * in the reference (its waits spin forever, v007:31-41). */
+FERRET_API int ferret_selftest_wait_timeout(unsigned long long timeout_ns, void* stream);
+
 /*
  * Routing -> expert-contiguous permutation (stable counting sort).
  * Replaces: the routing sort the reference takes from vLLM's
