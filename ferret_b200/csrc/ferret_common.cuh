@@ -123,6 +123,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Position in a ring of n slots: the slot and the parity of the current lap
+// (the mbarrier phase to wait for).  Advanced incrementally, so the pipeline
+// loops need no integer division by a runtime stage count.
+struct RingPos {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void advance(int n) {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {

@@ -211,15 +211,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_a = policy_evict_last();
             int it = 0;
+            RingPos rp;
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 int e, row0, rows, nb;
                 decode_tile<NT>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
                 const int wrow = e * N + nb * 128;
                 const int wrow_up = e * N + (N >> 1) + nb * 128;
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % NS;
-                    if (!mbar_wait(empty_bar(s), ((it / NS) & 1) ^ 1, abort_flag, args.ctl,
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl,
                                    SITE_EMPTY)) {
                         ok = false;
                         break;
@@ -240,14 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ================= MMA issuer =================
         if (elect_one()) {
             constexpr uint32_t idesc = make_idesc(128, NT, 0, 0);
-            int it = 0, ai = 0;
+            RingPos rs, ra;
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++it, ++ai) {
-                    const int s = it % NS, a = ai % C::kAcc;
-                    if (!mbar_wait(tempty_bar(a), ((ai / C::kAcc) & 1) ^ 1, abort_flag, args.ctl,
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(C::kAcc)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl,
                                    SITE_TEMPTY) ||
-                        !mbar_wait(full_bar(s), (it / NS) & 1, abort_flag, args.ctl, SITE_FULL)) {
+                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
                         ok = false;
                         break;
                     }

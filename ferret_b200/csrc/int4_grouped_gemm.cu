@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
             int it = 0;
+            RingPos rp;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 int e, row0, rows, nb;
@@ -222,9 +223,9 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                 for (int j = 0; j < NT; ++j)
                     tok[j] = j < rows ? __ldg(args.sorted_rows + row0 + j) / args.topk : 0;
                 const int ncol = nb * 128, ncol_up = (N >> 1) + nb * 128;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % NS;
-                    if (!mbar_wait(empty_bar(s), ((it / NS) & 1) ^ 1, abort_flag, args.ctl, I4_EMPTY)) {
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, I4_EMPTY)) {
                         ok = false;
                         break;
                     }
@@ -255,19 +256,19 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         // ================= MMA issuer =================
         if (elect_one()) {
             constexpr uint32_t idesc = make_idesc(128, NT, 1, 1);
-            int it = 0, tcount = 0;
+            RingPos rs, rd, ra;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tcount) {
-                const int a = tcount % C::kAcc;
-                if (!mbar_wait(te_bar(a), ((tcount / C::kAcc) & 1) ^ 1, abort_flag, args.ctl, I4_TE))
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ra.advance(C::kAcc)) {
+                const int a = ra.slot;
+                if (!mbar_wait(te_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, I4_TE))
                     break;
                 const uint32_t d_acc = tmem_base + a * C::kCols;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % NS, d = it % ND;
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), rd.advance(ND)) {
+                    const int s = rs.slot, d = rd.slot;
                     // the B tile comes straight from TMA; the dequantized A tile
                     // from the dequant warps
-                    if (!mbar_wait(full_bar(s), (it / NS) & 1, abort_flag, args.ctl, I4_FULL) ||
-                        !mbar_wait(dqf_bar(d), (it / ND) & 1, abort_flag, args.ctl, I4_DQF)) {
+                    if (!mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL) ||
+                        !mbar_wait(dqf_bar(d), rd.phase, abort_flag, args.ctl, I4_DQF)) {
                         ok = false;
                         break;
                     }
@@ -299,33 +300,45 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         // ================= dequant =================
         const int dt = tid - kDqWarp0 * 32;     // 0..255
         const int n = dt & 127, g0 = dt >> 7;   // groups g0 and g0 + 2
-        int it = 0;
+        RingPos rs, rd;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            for (int kb = 0; kb < nk; ++kb, ++it) {
-                const int s = it % NS, d = it % ND;
+            for (int kb = 0; kb < nk; ++kb, rs.advance(NS), rd.advance(ND)) {
+                const int s = rs.slot, d = rd.slot;
                 ok = __all_sync(0xffffffffu,
-                                mbar_wait(full_bar(s), (it / NS) & 1, abort_flag, args.ctl, I4_FULL) &&
-                                    mbar_wait(dqe_bar(d), ((it / ND) & 1) ^ 1, abort_flag, args.ctl, I4_DQE));
+                                mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL) &&
+                                    mbar_wait(dqe_bar(d), rd.phase ^ 1u, abort_flag, args.ctl, I4_DQE));
                 if (!ok) break;
                 const uint8_t* st = raw + s * C::kStage;
                 uint8_t* out_tile = dq + d * (C::kW * kDqTile);
+                // all shared loads first (they cannot be reordered past the
+                // stores below), then convert and store
+                uint32_t wv[C::kW][8], sv[C::kW][2];
 #pragma unroll
                 for (int w = 0; w < C::kW; ++w) {
                     const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kRawW);
                     const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + C::kW * kRawW + w * kRawS);
-                    uint8_t* tile = out_tile + w * kDqTile;
 #pragma unroll
                     for (int gi = 0; gi < 2; ++gi) {
                         const int g = g0 + 2 * gi;
-                        const uint32_t s1 = sc[g * 128 + n];
-                        const uint32_t s2 = s1 | (s1 << 16);
+                        sv[w][gi] = sc[g * 128 + n];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) wv[w][gi * 4 + q] = words[(g * 4 + q) * 128 + n];
+                    }
+                }
+#pragma unroll
+                for (int w = 0; w < C::kW; ++w) {
+                    uint8_t* tile = out_tile + w * kDqTile + n * 128;
+#pragma unroll
+                    for (int gi = 0; gi < 2; ++gi) {
+                        const int g = g0 + 2 * gi;
+                        const uint32_t s2 = sv[w][gi] | (sv[w][gi] << 16);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const int k8 = g * 4 + q;                    // 0..15
-                            const uint4 v = dequant_word(words[k8 * 128 + n], s2);
+                            const uint4 v = dequant_word(wv[w][gi * 4 + q], s2);
                             const int ac = k8 >> 3, c = k8 & 7;
-                            *reinterpret_cast<uint4*>(tile + ac * 16384 + n * 128 + ((c ^ (n & 7)) << 4)) = v;
+                            *reinterpret_cast<uint4*>(tile + ac * 16384 + ((c ^ (n & 7)) << 4)) = v;
                         }
                     }
                 }
@@ -338,13 +351,12 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         // ================= epilogue =================
         const int q = warp & 3;
         const int ldo = PAIR ? (N >> 1) : N;
-        int tcount = 0;
-        for (int t = blockIdx.x; t < total; t += gridDim.x, ++tcount) {
+        RingPos ra;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ra.advance(C::kAcc)) {
             int e, row0, rows, nb;
             i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
-            const int a = tcount % C::kAcc;
-            if (!__all_sync(0xffffffffu, mbar_wait(tf_bar(a), (tcount / C::kAcc) & 1, abort_flag,
-                                                   args.ctl, I4_TF)))
+            const int a = ra.slot;
+            if (!__all_sync(0xffffffffu, mbar_wait(tf_bar(a), ra.phase, abort_flag, args.ctl, I4_TF)))
                 break;
             tc_fence_after();
             const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * C::kCols;
