@@ -11,17 +11,18 @@
 //
 // tcgen05 has no INT4 operand type, so the weights are dequantized on chip:
 //   * warp 0 (TMA): per 128-wide K block, the packed weight box (128 n x 16
-//     int32 = 8 KB), its bf16 scales (128 n x 4 groups = 1 KB) and, one
-//     128-byte box per token row, the activation rows of the tile straight
-//     from `hidden` (no gather pass) into an NS-deep ring;
-//   * warps 2-9 (dequant, 256 threads): each thread turns 4 packed words of
+//     int32 = 8 KB) and its bf16 scales (128 n x 4 groups = 1 KB) from lane 0,
+//     and, one 128-byte box per token row issued by that row's lane, the
+//     activation rows of the tile straight from `hidden` (no gather pass),
+//     into an NS-deep ring;
+//   * warps 2-17 (dequant, 512 threads): each thread turns 4 packed words of
 //     one weight row (32 K values, one scale) into four 16-byte bf16 chunks,
 //     written into the 128-byte-swizzled K-major layout the MMA reads, in a
 //     second, shallower ring;
 //   * warp 1 (MMA): tcgen05.mma.kind::f16 (bf16 x bf16 -> f32), M = 128 weight
 //     rows, N = NT token rows (swap-AB), K = 16, accumulating the whole K
 //     range in one TMEM buffer per tile (double-buffered across tiles);
-//   * warps 10-13 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
+//   * warps 18-21 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
 // The dequant arithmetic is exact: nibble pairs become bf16 (128 + n) with one
 // lop3 against the 0x4300 exponent, minus 136 gives n - 8 exactly, and one
 // bf16x2 multiply by the scale rounds once -- the oracle's bf16((n-8)*s).
@@ -34,9 +35,9 @@
 namespace ferret {
 namespace {
 
-constexpr int kI4Threads = 448;      // 14 warps
-constexpr int kDqWarp0 = 2, kDqWarps = 8, kDqThreads = kDqWarps * 32;
-constexpr int kEpiWarp0 = 10, kI4EpiThreads = 128;
+constexpr int kDqWarp0 = 2, kDqWarps = 16, kDqThreads = kDqWarps * 32;
+constexpr int kEpiWarp0 = kDqWarp0 + kDqWarps, kI4EpiThreads = 128;
+constexpr int kI4Threads = (kEpiWarp0 + 4) * 32;   // 22 warps
 constexpr int kI4MaxE = 1024;
 constexpr int kI4MaxStages = 16, kI4MaxDq = 4, kI4MaxAcc = 4;
 constexpr int kRawW = 128 * 16 * 4;    // packed box: 128 n x 16 words
@@ -205,31 +206,31 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     const int total = mt_start[E] * nbc;
 
     if (warp == 0) {
-        // ================= TMA producer =================
-        if (elect_one()) {
+        // ================= TMA producer (whole warp) =================
+        // lane 0 loads the weight and scale boxes; lane j < rows loads token row
+        // j, so the per-row boxes are issued in parallel, not one by one.
+        if (lane == 0) {
             tma_prefetch_desc(&tm_w);
             tma_prefetch_desc(&tm_s);
             tma_prefetch_desc(&tm_x);
-            const uint64_t pol_w = policy_evict_first();
-            const uint64_t pol_x = policy_evict_last();
-            int it = 0;
-            RingPos rp;
-            bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                int e, row0, rows, nb;
-                i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
-                int tok[NT];
-#pragma unroll
-                for (int j = 0; j < NT; ++j)
-                    tok[j] = j < rows ? __ldg(args.sorted_rows + row0 + j) / args.topk : 0;
-                const int ncol = nb * 128, ncol_up = (N >> 1) + nb * 128;
-                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
-                    const int s = rp.slot;
-                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, I4_EMPTY)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t st = raw_base + s * C::kStage;
+        }
+        const uint64_t pol_w = policy_evict_first();
+        const uint64_t pol_x = policy_evict_last();
+        int it = 0;
+        RingPos rp;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            int e, row0, rows, nb;
+            i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
+            const int tok = lane < rows ? __ldg(args.sorted_rows + row0 + lane) / args.topk : 0;
+            const int ncol = nb * 128, ncol_up = (N >> 1) + nb * 128;
+            for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                const int s = rp.slot;
+                ok = __all_sync(0xffffffffu, mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag,
+                                                       args.ctl, I4_EMPTY));
+                if (!ok) break;
+                const uint32_t st = raw_base + s * C::kStage;
+                if (lane == 0) {
                     mbar_expect_tx(full_bar(s), C::kW * (kRawW + kRawS) + rows * 256);
                     tma_load_2d_hint(st, &tm_w, ncol, e * kq + kb * 16, full_bar(s), pol_w);
                     tma_load_2d_hint(st + C::kW * kRawW, &tm_s, ncol, e * kg + kb * 4, full_bar(s), pol_w);
@@ -238,20 +239,19 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                         tma_load_2d_hint(st + C::kW * kRawW + kRawS, &tm_s, ncol_up, e * kg + kb * 4,
                                          full_bar(s), pol_w);
                     }
-                    const uint32_t bt = st + C::kW * (kRawW + kRawS);
-#pragma unroll
-                    for (int j = 0; j < NT; ++j) {
-                        if (j < rows) {
-                            tma_load_2d_hint(bt + j * 128, &tm_x, kb * 128, tok[j], full_bar(s), pol_x);
-                            tma_load_2d_hint(bt + NT * 128 + j * 128, &tm_x, kb * 128 + 64, tok[j],
-                                             full_bar(s), pol_x);
-                        }
-                    }
+                }
+                __syncwarp();
+                if (lane < rows) {
+                    const uint32_t bt = st + C::kW * (kRawW + kRawS) + lane * 128;
+                    tma_load_2d_hint(bt, &tm_x, kb * 128, tok, full_bar(s), pol_x);
+                    tma_load_2d_hint(bt + NT * 128, &tm_x, kb * 128 + 64, tok, full_bar(s), pol_x);
                 }
             }
+        }
+        // drain: the last load issued into each stage may still be in flight
+        if (lane == 0)
             for (int i = max(0, it - NS); i < it; ++i)
                 mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, I4_DRAIN, false);
-        }
     } else if (warp == 1) {
         // ================= MMA issuer =================
         if (elect_one()) {
@@ -298,8 +298,8 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         }
     } else if (warp < kEpiWarp0) {
         // ================= dequant =================
-        const int dt = tid - kDqWarp0 * 32;     // 0..255
-        const int n = dt & 127, g0 = dt >> 7;   // groups g0 and g0 + 2
+        const int dt = tid - kDqWarp0 * 32;
+        constexpr int kUnits = 512 / kDqThreads;   // (scale group, weight row) units per thread
         RingPos rs, rd;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -313,30 +313,30 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                 uint8_t* out_tile = dq + d * (C::kW * kDqTile);
                 // all shared loads first (they cannot be reordered past the
                 // stores below), then convert and store
-                uint32_t wv[C::kW][8], sv[C::kW][2];
+                uint32_t wv[C::kW][kUnits][4], sv[C::kW][kUnits];
 #pragma unroll
                 for (int w = 0; w < C::kW; ++w) {
                     const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kRawW);
                     const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + C::kW * kRawW + w * kRawS);
 #pragma unroll
-                    for (int gi = 0; gi < 2; ++gi) {
-                        const int g = g0 + 2 * gi;
-                        sv[w][gi] = sc[g * 128 + n];
+                    for (int ui = 0; ui < kUnits; ++ui) {
+                        const int u = dt + ui * kDqThreads, g = u >> 7, n = u & 127;
+                        sv[w][ui] = sc[g * 128 + n];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) wv[w][gi * 4 + q] = words[(g * 4 + q) * 128 + n];
+                        for (int q = 0; q < 4; ++q) wv[w][ui][q] = words[(g * 4 + q) * 128 + n];
                     }
                 }
 #pragma unroll
                 for (int w = 0; w < C::kW; ++w) {
-                    uint8_t* tile = out_tile + w * kDqTile + n * 128;
 #pragma unroll
-                    for (int gi = 0; gi < 2; ++gi) {
-                        const int g = g0 + 2 * gi;
-                        const uint32_t s2 = sv[w][gi] | (sv[w][gi] << 16);
+                    for (int ui = 0; ui < kUnits; ++ui) {
+                        const int u = dt + ui * kDqThreads, g = u >> 7, n = u & 127;
+                        uint8_t* tile = out_tile + w * kDqTile + n * 128;
+                        const uint32_t s2 = sv[w][ui] | (sv[w][ui] << 16);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const int k8 = g * 4 + q;                    // 0..15
-                            const uint4 v = dequant_word(wv[w][gi * 4 + q], s2);
+                            const uint4 v = dequant_word(wv[w][ui][q], s2);
                             const int ac = k8 >> 3, c = k8 & 7;
                             *reinterpret_cast<uint4*>(tile + ac * 16384 + ((c ^ (n & 7)) << 4)) = v;
                         }
@@ -360,35 +360,33 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                 break;
             tc_fence_after();
             const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * C::kCols;
-            float g[NT], u[PAIR ? NT : 1];
+            const int ncol = nb * 128 + q * 32 + lane;
+            // 8 token columns at a time: few live registers
 #pragma unroll
             for (int c = 0; c < NT; c += 8) {
-                uint32_t r[8];
+                uint32_t r[8], v[8];
                 asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                                "=r"(r[6]), "=r"(r[7])
                              : "r"(tb + c));
-#pragma unroll
-                for (int j = 0; j < 8; ++j) g[c + j] = __uint_as_float(r[j]);
-                if (PAIR) {
+                if (PAIR)
                     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
-                                   "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]),
+                                   "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                                  : "r"(tb + NT + c));
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) u[PAIR ? c + j : 0] = __uint_as_float(r[j]);
+                tmem_ld_wait();
+                if (c + 8 >= NT) {
+                    tc_fence_before();
+                    mbar_arrive(te_bar(a));      // the accumulator is free for the next tile
                 }
-            }
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(te_bar(a));
-            const int ncol = nb * 128 + q * 32 + lane;
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                if (j < rows) {
-                    const int orow = __ldg(args.sorted_rows + row0 + j);
-                    const float v = PAIR ? silu_mul(g[j], u[PAIR ? j : 0]) : g[j];
-                    args.out[(size_t)orow * ldo + ncol] = __float2bfloat16_rn(v);
+                for (int j = 0; j < 8; ++j) {
+                    if (c + j < rows) {
+                        const int orow = __ldg(args.sorted_rows + row0 + c + j);
+                        const float g = __uint_as_float(r[j]);
+                        const float val = PAIR ? silu_mul(g, __uint_as_float(v[j])) : g;
+                        args.out[(size_t)orow * ldo + ncol] = __float2bfloat16_rn(val);
+                    }
                 }
             }
         }
