@@ -311,20 +311,22 @@ def run_single_int4(args, cfg):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     raw, scales = data.int4_weights(cfg.E, cfg.N, cfg.K, device=dev)
-    packed = ops.int4_repack_w13(raw)
-    del raw
+    packed = ops.Int4W13Weights(raw, scales)
+    del raw, scales
     hidden = data.activations(cfg.T, cfg.K).to(dev)
     ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
     n_out = cfg.N // 2 if cfg.silu else cfg.N
     out = torch.zeros(cfg.R, n_out, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(ops.lib().ferret_int4_moe_w13_workspace_size(cfg.T, cfg.topk, cfg.K),
+                     dtype=torch.uint8, device=dev)
 
     def step():
-        ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out)
+        ops.moe_wna16_w13(hidden, packed, ids, silu=cfg.silu, out=out, workspace=ws)
 
     if args.gemm_only:
         perm = ops.moe_permute(ids, cfg.E)
         for _ in range(args.gemm_only):
-            ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out, perm=perm)
+            ops.moe_wna16_w13(hidden, packed, ids, silu=cfg.silu, out=out, perm=perm, workspace=ws)
         torch.cuda.synchronize()
         return None
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -349,8 +351,8 @@ def run_single_int4(args, cfg):
     step_ms = timed(step, args.steps)
     clk = clocks.stop()
     perm = ops.moe_permute(ids, cfg.E)
-    gemm_ms = timed(lambda: ops.moe_wna16_w13(hidden, packed, scales, ids, silu=cfg.silu, out=out,
-                                              perm=perm), args.steps)
+    gemm_ms = timed(lambda: ops.moe_wna16_w13(hidden, packed, ids, silu=cfg.silu, out=out,
+                                              perm=perm, workspace=ws), args.steps)
     h_hidden, h_ids = hidden.cpu().pin_memory(), ids.cpu().pin_memory()
     h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     d_hidden, d_ids = torch.empty_like(hidden), torch.empty_like(ids)
@@ -358,7 +360,7 @@ def run_single_int4(args, cfg):
     def e2e():
         d_hidden.copy_(h_hidden, non_blocking=True)
         d_ids.copy_(h_ids, non_blocking=True)
-        ops.moe_wna16_w13(d_hidden, packed, scales, d_ids, silu=cfg.silu, out=out)
+        ops.moe_wna16_w13(d_hidden, packed, d_ids, silu=cfg.silu, out=out, workspace=ws)
         h_out.copy_(out, non_blocking=True)
     e2e_ms = timed(e2e, args.steps)
     if ops.last_device_status() != 0:

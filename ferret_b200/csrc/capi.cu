@@ -101,6 +101,23 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
     return r == CUDA_SUCCESS ? FERRET_OK : FERRET_ERR_CUDA;
 }
 
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
+                 bool swizzle128) {
+    std::call_once(g_encode_once, resolve_encode);
+    if (!g_encode) return FERRET_ERR_UNSUPPORTED;
+    if (dims[0] == 0 || dims[1] == 0 || dims[2] == 0) return FERRET_ERR_SHAPE;
+    cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+    cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), d, st, bx, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FERRET_OK : FERRET_ERR_CUDA;
+}
+
 }  // namespace ferret
 
 using namespace ferret;

@@ -33,6 +33,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                  uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_cols,
                  uint32_t box_rows, bool swizzle128);
 
+// 3-D tensor map: dims[0] innermost (elements), byte strides of dims 1 and 2,
+// box[0..2]; 128-byte swizzle when swizzle128.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
+                 bool swizzle128);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

@@ -164,6 +164,27 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap
         : "memory");
 }
 
+// 3-D tiled load (same completion rule as the 2-D form).
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const CUtensorMap* m, int x, int y,
+                                                 int z, uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+// Contiguous bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes,
+                                               uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

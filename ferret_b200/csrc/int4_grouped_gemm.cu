@@ -9,25 +9,27 @@
 // with p the flat (token, slot) index; rows are written in that (token, slot)
 // order, as Marlin writes them.
 //
-// tcgen05 has no INT4 operand type, so the weights are dequantized on chip:
-//   * warp 0 (TMA): per 128-wide K block, the packed weight box (128 n x 16
-//     int32 = 8 KB) and its bf16 scales (128 n x 4 groups = 1 KB) from lane 0,
-//     and, one 128-byte box per token row issued by that row's lane, the
-//     activation rows of the tile straight from `hidden` (no gather pass),
-//     into an NS-deep ring;
+// Data path, designed so each 128-wide K block costs three copy operations (the
+// per-SM copy engine, not HBM, limits a design that issues one small copy per
+// activation row and separate scale boxes):
+//   * load time (ferret_int4_repack_w13): every 128 (n) x 128 (k) weight block
+//     and its 128 x 4 bf16 group scales become one contiguous 9 KB blob, nibbles
+//     reordered so each (k, k+1) pair sits 16 bits apart;
+//   * per call, a gather pass writes the expert-sorted activation rows
+//     contiguously (workspace), so one tensor-map box brings NT token rows of
+//     a 64-wide K half in the 128-byte-swizzled layout;
+//   * warp 0 (one thread): per K block, one bulk copy of the weight blob (two
+//     with SiLU: gate and up) and two B-tile boxes into an NS-deep ring;
 //   * warps 2-17 (dequant, 512 threads): each thread turns 4 packed words of
-//     one weight row (32 K values, one scale) into four 16-byte bf16 chunks,
-//     written into the 128-byte-swizzled K-major layout the MMA reads, in a
-//     second, shallower ring;
+//     one weight row (32 K values, one scale) into four 16-byte bf16 chunks in
+//     the swizzled K-major layout the MMA reads, in a shallower second ring;
 //   * warp 1 (MMA): tcgen05.mma.kind::f16 (bf16 x bf16 -> f32), M = 128 weight
-//     rows, N = NT token rows (swap-AB), K = 16, accumulating the whole K
-//     range in one TMEM buffer per tile (double-buffered across tiles);
+//     rows, N = NT token rows (swap-AB), K = 16, accumulating the whole K range
+//     in one TMEM buffer per tile (double-buffered across tiles);
 //   * warps 18-21 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
 // The dequant arithmetic is exact: nibble pairs become bf16 (128 + n) with one
 // lop3 against the 0x4300 exponent, minus 136 gives n - 8 exactly, and one
 // bf16x2 multiply by the scale rounds once -- the oracle's bf16((n-8)*s).
-// For that the nibbles of each word are pre-permuted once at load time
-// (ferret_int4_repack_w13) so that the pairs (k, k+1) sit 16 bits apart.
 #include <algorithm>
 
 #include "capi_internal.h"
@@ -40,13 +42,15 @@ constexpr int kEpiWarp0 = kDqWarp0 + kDqWarps, kI4EpiThreads = 128;
 constexpr int kI4Threads = (kEpiWarp0 + 4) * 32;   // 22 warps
 constexpr int kI4MaxE = 1024;
 constexpr int kI4MaxStages = 16, kI4MaxDq = 4, kI4MaxAcc = 4;
-constexpr int kRawW = 128 * 16 * 4;    // packed box: 128 n x 16 words
-constexpr int kRawS = 128 * 4 * 2;     // scales: 128 n x 4 groups bf16
+constexpr int kRawW = 128 * 16 * 4;    // packed words: 16 k8 rows x 128 n
+constexpr int kRawS = 128 * 4 * 2;     // scales: 4 groups x 128 n bf16
+constexpr int kBlob = kRawW + kRawS;   // 9216 B per 128 x 128 weight block
 constexpr int kDqTile = 128 * 128 * 2; // bf16 128 n x 128 k (two 64-wide atoms)
 
 enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_DQE = 3, I4_DQF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7 };
 
 struct Int4Args {
+    const uint8_t* blob;          // [E][N/128][K/128] x kBlob
     const int32_t* sorted_rows;   // flat (token, slot) of each expert-sorted row
     const int32_t* offsets;       // [E+1]
     __nv_bfloat16* out;
@@ -59,7 +63,7 @@ template <int NT, bool PAIR>
 struct I4Cfg {
     static constexpr int kW = PAIR ? 2 : 1;
     static constexpr int kBTile = NT * 256;                     // NT rows x 128 k bf16
-    static constexpr int kStage = kW * (kRawW + kRawS) + kBTile;
+    static constexpr int kStage = kW * kBlob + kBTile;          // multiple of 1024
     static constexpr int kCols = NT * kW;
     static constexpr int kAcc = 2;
     static constexpr int kUsed = kAcc * kCols;
@@ -141,9 +145,7 @@ __device__ __forceinline__ void i4_decode_tile(int t, int nbc, int E, const int*
 
 template <int NT, bool PAIR>
 __global__ void __launch_bounds__(kI4Threads, 1)
-    int4_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_w,
-                            const __grid_constant__ CUtensorMap tm_s,
-                            const __grid_constant__ CUtensorMap tm_x, const Int4Args args) {
+    int4_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const Int4Args args) {
     using C = I4Cfg<NT, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
@@ -151,7 +153,6 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     const int N = args.N, K = args.K, E = args.E, NS = args.stages, ND = args.dq_stages;
     const int nk = K >> 7;
     const int nbc = PAIR ? (N >> 8) : (N >> 7);
-    const int kq = K >> 3, kg = K >> 5;     // packed rows / scale rows per expert
     const I4Layout L = i4_layout(C::kStage, NS, C::kW * kDqTile, ND, E);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
     int* part = reinterpret_cast<int*>(smem + L.part_off);
@@ -193,8 +194,9 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     bool seg_bad = false;
     for (int e = tid; e < E; e += kI4Threads) {
         const int s = args.offsets[e], c = args.offsets[e + 1] - s;
-        if (s < 0 || c < 0 || s + c > args.R) seg_bad = true;
-        mt_start[e] = (s < 0 || c < 0 || s + c > args.R) ? 0 : (c + NT - 1) / NT;
+        const bool bad = s < 0 || c < 0 || s + c > args.R;
+        seg_bad |= bad;
+        mt_start[e] = bad ? 0 : (c + NT - 1) / NT;
     }
     if (seg_bad) report(args.ctl, DEV_LAYOUT);
     __syncthreads();
@@ -204,54 +206,41 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int total = mt_start[E] * nbc;
+    const size_t blob_nb = (size_t)(K >> 7) * kBlob;          // bytes per (e, n-block)
 
     if (warp == 0) {
-        // ================= TMA producer (whole warp) =================
-        // lane 0 loads the weight and scale boxes; lane j < rows loads token row
-        // j, so the per-row boxes are issued in parallel, not one by one.
-        if (lane == 0) {
-            tma_prefetch_desc(&tm_w);
-            tma_prefetch_desc(&tm_s);
-            tma_prefetch_desc(&tm_x);
-        }
-        const uint64_t pol_w = policy_evict_first();
-        const uint64_t pol_x = policy_evict_last();
-        int it = 0;
-        RingPos rp;
-        bool ok = true;
-        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            int e, row0, rows, nb;
-            i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
-            const int tok = lane < rows ? __ldg(args.sorted_rows + row0 + lane) / args.topk : 0;
-            const int ncol = nb * 128, ncol_up = (N >> 1) + nb * 128;
-            for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
-                const int s = rp.slot;
-                ok = __all_sync(0xffffffffu, mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag,
-                                                       args.ctl, I4_EMPTY));
-                if (!ok) break;
-                const uint32_t st = raw_base + s * C::kStage;
-                if (lane == 0) {
-                    mbar_expect_tx(full_bar(s), C::kW * (kRawW + kRawS) + rows * 256);
-                    tma_load_2d_hint(st, &tm_w, ncol, e * kq + kb * 16, full_bar(s), pol_w);
-                    tma_load_2d_hint(st + C::kW * kRawW, &tm_s, ncol, e * kg + kb * 4, full_bar(s), pol_w);
-                    if (PAIR) {
-                        tma_load_2d_hint(st + kRawW, &tm_w, ncol_up, e * kq + kb * 16, full_bar(s), pol_w);
-                        tma_load_2d_hint(st + C::kW * kRawW + kRawS, &tm_s, ncol_up, e * kg + kb * 4,
-                                         full_bar(s), pol_w);
+        // ================= copy producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_a = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
+                const uint8_t* wg = args.blob + ((size_t)e * (N >> 7) + nb) * blob_nb;
+                const uint8_t* wu = args.blob + ((size_t)e * (N >> 7) + (N >> 8) + nb) * blob_nb;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, I4_EMPTY)) {
+                        ok = false;
+                        break;
                     }
-                }
-                __syncwarp();
-                if (lane < rows) {
-                    const uint32_t bt = st + C::kW * (kRawW + kRawS) + lane * 128;
-                    tma_load_2d_hint(bt, &tm_x, kb * 128, tok, full_bar(s), pol_x);
-                    tma_load_2d_hint(bt + NT * 128, &tm_x, kb * 128 + 64, tok, full_bar(s), pol_x);
+                    const uint32_t st = raw_base + s * C::kStage;
+                    mbar_expect_tx(full_bar(s), C::kStage);
+                    bulk_load_hint(st, wg + (size_t)kb * kBlob, kBlob, full_bar(s), pol_w);
+                    if (PAIR) bulk_load_hint(st + kBlob, wu + (size_t)kb * kBlob, kBlob, full_bar(s), pol_w);
+                    tma_load_2d_hint(st + C::kW * kBlob, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(st + C::kW * kBlob + NT * 128, &tm_a, kb * 128 + 64, row0,
+                                     full_bar(s), pol_a);
                 }
             }
-        }
-        // drain: the last load issued into each stage may still be in flight
-        if (lane == 0)
+            // drain: the last load issued into each stage may still be in flight
             for (int i = max(0, it - NS); i < it; ++i)
                 mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, I4_DRAIN, false);
+        }
     } else if (warp == 1) {
         // ================= MMA issuer =================
         if (elect_one()) {
@@ -260,20 +249,19 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ra.advance(C::kAcc)) {
                 const int a = ra.slot;
-                if (!mbar_wait(te_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, I4_TE))
-                    break;
+                if (!mbar_wait(te_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, I4_TE)) break;
                 const uint32_t d_acc = tmem_base + a * C::kCols;
                 for (int kb = 0; kb < nk; ++kb, rs.advance(NS), rd.advance(ND)) {
                     const int s = rs.slot, d = rd.slot;
-                    // the B tile comes straight from TMA; the dequantized A tile
-                    // from the dequant warps
+                    // the B tile comes straight from the copy engine; the
+                    // dequantized A tile from the dequant warps
                     if (!mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL) ||
                         !mbar_wait(dqf_bar(d), rd.phase, abort_flag, args.ctl, I4_DQF)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t bt = raw_base + s * C::kStage + C::kW * (kRawW + kRawS);
+                    const uint32_t bt = raw_base + s * C::kStage + C::kW * kBlob;
                     const uint32_t wt = dq_base + d * (C::kW * kDqTile);
 #pragma unroll
                     for (int ac = 0; ac < 2; ++ac) {
@@ -316,8 +304,8 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                 uint32_t wv[C::kW][kUnits][4], sv[C::kW][kUnits];
 #pragma unroll
                 for (int w = 0; w < C::kW; ++w) {
-                    const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kRawW);
-                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + C::kW * kRawW + w * kRawS);
+                    const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kBlob);
+                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + w * kBlob + kRawW);
 #pragma unroll
                     for (int ui = 0; ui < kUnits; ++ui) {
                         const int u = dt + ui * kDqThreads, g = u >> 7, n = u & 127;
@@ -401,37 +389,69 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     }
 }
 
-// Load-time nibble permutation: slot i of each word receives K offset
-// perm[i] = {0,2,4,6,1,3,5,7}[i], so (k, k+1) pairs are 16 bits apart.
-__global__ void int4_repack_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
-                                   size_t words) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words;
+// Load-time repack into 9 KB blobs: block (e, nb, kb) = 2048 words
+// [k8][n] with the nibbles of each word reordered to K offsets
+// {0,2,4,6,1,3,5,7}, then 4 x 128 bf16 scales [g][n].
+__global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint16_t* __restrict__ sc,
+                                   uint32_t* __restrict__ blob, int E, int K, int N) {
+    const int nbn = N >> 7, nbk = K >> 7;
+    const size_t words_per_block = kBlob / 4;                 // 2304
+    const size_t total = (size_t)E * nbn * nbk * words_per_block;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (size_t)gridDim.x * blockDim.x) {
-        const uint32_t w = in[i];
-        uint32_t r = 0;
+        const size_t b = i / words_per_block;
+        const int w = (int)(i - b * words_per_block);
+        const int kb = (int)(b % nbk);
+        const int nb = (int)((b / nbk) % nbn);
+        const int e = (int)(b / ((size_t)nbk * nbn));
+        uint32_t r;
+        if (w < 2048) {
+            const int k8 = w >> 7, n = w & 127;
+            const uint32_t v = raw[((size_t)e * (K >> 3) + kb * 16 + k8) * N + nb * 128 + n];
+            r = 0;
 #pragma unroll
-        for (int slot = 0; slot < 8; ++slot) {
-            const int k = slot < 4 ? 2 * slot : 2 * (slot - 4) + 1;
-            r |= ((w >> (4 * k)) & 0xFu) << (4 * slot);
+            for (int slot = 0; slot < 8; ++slot) {
+                const int k = slot < 4 ? 2 * slot : 2 * (slot - 4) + 1;
+                r |= ((v >> (4 * k)) & 0xFu) << (4 * slot);
+            }
+        } else {
+            const int idx = (w - 2048) * 2, g = idx >> 7, n = idx & 127;
+            const size_t src = ((size_t)e * (K >> 5) + kb * 4 + g) * N + nb * 128 + n;
+            r = (uint32_t)sc[src] | ((uint32_t)sc[src + 1] << 16);
         }
-        out[i] = r;
+        blob[i] = r;
+    }
+}
+
+// Expert-sorted activation rows: out[r] = hidden[rows[r] / topk]
+// (zero row for a negative entry or a token >= T, the latter reported).
+__global__ void gather_rows_kernel(const uint4* __restrict__ hidden, const int32_t* __restrict__ rows,
+                                   int topk, int T, int R, int K, uint4* __restrict__ out,
+                                   DevCtl ctl) {
+    const int per_row = K >> 3;                                // 16-byte chunks
+    const size_t total = (size_t)R * per_row;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / per_row), c = (int)(i - (size_t)r * per_row);
+        const int src = rows[r];
+        int tok = src < 0 ? -1 : src / topk;
+        if (tok >= T) {
+            if (c == 0) report(ctl, DEV_BAD_ROW);
+            tok = -1;
+        }
+        out[i] = tok < 0 ? make_uint4(0, 0, 0, 0) : hidden[(size_t)tok * per_row + c];
     }
 }
 
 template <int NT, bool PAIR>
-int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_packed,
-                const void* scales, const int32_t* sorted_rows, const int32_t* offsets, void* out,
-                int T, int topk, int N, int K, int E, int R, cudaStream_t stream) {
+int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blob,
+                const int32_t* sorted_rows, const int32_t* offsets, void* out, int T, int topk,
+                int N, int K, int E, int R, cudaStream_t stream) {
     using C = I4Cfg<NT, PAIR>;
-    CUtensorMap tm_w, tm_s, tm_x;
-    int rc = make_tmap_2d(&tm_w, w_packed, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, (uint64_t)E * (K / 8), N,
-                          (uint64_t)N * 4, 128, 16, false);
-    if (rc != FERRET_OK) return rc;
-    rc = make_tmap_2d(&tm_s, scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E * (K / 32), N,
-                      (uint64_t)N * 2, 128, 4, false);
-    if (rc != FERRET_OK) return rc;
-    rc = make_tmap_2d(&tm_x, hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K, (uint64_t)K * 2, 64, 1,
-                      true);
+    CUtensorMap tm_a;
+    // gathered activations [R, K] bf16, box = 64 K values x NT rows
+    int rc = make_tmap_2d(&tm_a, a_sorted, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, (uint64_t)K * 2,
+                          64, NT, true);
     if (rc != FERRET_OK) return rc;
     const int budget = info->max_smem_optin - 1024;
     const int dq_bytes = C::kW * kDqTile;
@@ -447,6 +467,7 @@ int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_pac
         return FERRET_ERR_CUDA;
     }
     Int4Args a;
+    a.blob = blob;
     a.sorted_rows = sorted_rows;
     a.offsets = offsets;
     a.out = static_cast<__nv_bfloat16*>(out);
@@ -459,7 +480,7 @@ int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_pac
     a.stages = stages;
     a.dq_stages = nd;
     a.ctl = make_ctl(info);
-    kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_w, tm_s, tm_x, a);
+    kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_a, a);
     return launch_status();
 }
 
@@ -468,33 +489,49 @@ int launch_int4(const DeviceInfo* info, const void* hidden, const int32_t* w_pac
 
 using namespace ferret;
 
-extern "C" int ferret_int4_repack_w13(const int32_t* w_raw, int32_t* w_packed, int E, int K, int N,
-                                      void* stream) {
-    if (E <= 0 || K <= 0 || N <= 0 || K % 8) return FERRET_ERR_SHAPE;
-    if (!w_raw || !w_packed) return FERRET_ERR_NULL;
+extern "C" size_t ferret_int4_blob_bytes(int E, int K, int N) {
+    if (E <= 0 || K <= 0 || N <= 0 || K % 128 || N % 128) return 0;
+    return (size_t)E * (N / 128) * (K / 128) * kBlob;
+}
+
+extern "C" size_t ferret_int4_moe_w13_workspace_size(int T, int topk, int K) {
+    if (T < 0 || topk <= 0 || K <= 0) return 0;
+    return (size_t)T * topk * K * 2;
+}
+
+extern "C" int ferret_int4_repack_w13(const int32_t* w_raw, const void* w_scale_bf16, void* w_blob,
+                                      int E, int K, int N, void* stream) {
+    if (E <= 0 || K <= 0 || N <= 0 || K % 128 || N % 128) return FERRET_ERR_SHAPE;
+    if (!w_raw || !w_scale_bf16 || !w_blob) return FERRET_ERR_NULL;
+    if (!aligned16(w_blob) || (reinterpret_cast<uintptr_t>(w_raw) & 3u) ||
+        (reinterpret_cast<uintptr_t>(w_scale_bf16) & 3u))
+        return FERRET_ERR_ALIGN;
     DeviceInfo* info = nullptr;
     int rc = current_device(&info);
     if (rc != FERRET_OK) return rc;
-    const size_t words = (size_t)E * (K / 8) * N;
+    const size_t words = ferret_int4_blob_bytes(E, K, N) / 4;
     const int grid = (int)std::min<size_t>((words + 255) / 256, (size_t)info->num_sms * 16);
     int4_repack_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint32_t*>(w_raw), reinterpret_cast<uint32_t*>(w_packed), words);
+        reinterpret_cast<const uint32_t*>(w_raw), static_cast<const uint16_t*>(w_scale_bf16),
+        static_cast<uint32_t*>(w_blob), E, K, N);
     return launch_status();
 }
 
-extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const int32_t* w_packed,
-                                   const void* w_scale_bf16, const int32_t* sorted_rows,
-                                   const int32_t* expert_offsets, void* out_bf16, int T, int topk,
-                                   int N, int K, int E, int flags, void* stream) {
+extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
+                                   const int32_t* sorted_rows, const int32_t* expert_offsets,
+                                   void* out_bf16, int T, int topk, int N, int K, int E, int flags,
+                                   void* workspace, size_t ws_bytes, void* stream) {
     const bool pair = (flags & FERRET_SILU_MUL) != 0;
     if (T < 0 || topk <= 0 || N <= 0 || K <= 0 || E <= 0 || E > kI4MaxE) return FERRET_ERR_SHAPE;
     if (K % 128 || N % 128 || (pair && N % 256)) return FERRET_ERR_SHAPE;
-    if ((long long)E * (K / 8) >= (1ll << 31) || (long long)T * topk >= (1ll << 31))
+    if ((long long)T * topk >= (1ll << 31) || (long long)E * (N / 128) * (K / 128) >= (1ll << 31))
         return FERRET_ERR_SHAPE;
     if (T == 0) return FERRET_OK;
-    if (!hidden_bf16 || !w_packed || !w_scale_bf16 || !sorted_rows || !expert_offsets || !out_bf16)
+    if (!hidden_bf16 || !w_blob || !sorted_rows || !expert_offsets || !out_bf16)
         return FERRET_ERR_NULL;
-    if (!aligned16(hidden_bf16) || !aligned16(w_packed) || !aligned16(w_scale_bf16) ||
+    if (!workspace || ws_bytes < ferret_int4_moe_w13_workspace_size(T, topk, K))
+        return FERRET_ERR_WORKSPACE;
+    if (!aligned16(hidden_bf16) || !aligned16(w_blob) || !aligned16(workspace) ||
         (reinterpret_cast<uintptr_t>(out_bf16) & 1u))
         return FERRET_ERR_ALIGN;
     DeviceInfo* info = nullptr;
@@ -502,28 +539,32 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const int32_t* w_pac
     if (rc != FERRET_OK) return rc;
     cudaStream_t s = as_stream(stream);
     const int R = T * topk;
+    {
+        const size_t chunks = (size_t)R * (K / 8);
+        const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)info->num_sms * 8);
+        gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(hidden_bf16), sorted_rows,
+                                                topk, T, R, K, static_cast<uint4*>(workspace),
+                                                make_ctl(info));
+        if ((rc = launch_status()) != FERRET_OK) return rc;
+    }
+    const uint8_t* blob = static_cast<const uint8_t*>(w_blob);
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
     if (nt == 0) {
         const int avg = (R + E - 1) / E;
         nt = avg <= 4 ? 8 : avg <= 12 ? 16 : 32;
     }
+#define FERRET_I4_CASE(NT_)                                                                        \
+    case NT_:                                                                                      \
+        return pair ? launch_int4<NT_, true>(info, workspace, blob, sorted_rows, expert_offsets,   \
+                                             out_bf16, T, topk, N, K, E, R, s)                     \
+                    : launch_int4<NT_, false>(info, workspace, blob, sorted_rows, expert_offsets,  \
+                                              out_bf16, T, topk, N, K, E, R, s);
     switch (nt) {
-        case 8:
-            return pair ? launch_int4<8, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                               expert_offsets, out_bf16, T, topk, N, K, E, R, s)
-                        : launch_int4<8, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s);
-        case 16:
-            return pair ? launch_int4<16, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s)
-                        : launch_int4<16, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                                 expert_offsets, out_bf16, T, topk, N, K, E, R, s);
-        case 32:
-            return pair ? launch_int4<32, true>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                                expert_offsets, out_bf16, T, topk, N, K, E, R, s)
-                        : launch_int4<32, false>(info, hidden_bf16, w_packed, w_scale_bf16, sorted_rows,
-                                                 expert_offsets, out_bf16, T, topk, N, K, E, R, s);
+        FERRET_I4_CASE(8)
+        FERRET_I4_CASE(16)
+        FERRET_I4_CASE(32)
         default:
             return FERRET_ERR_SHAPE;
     }
+#undef FERRET_I4_CASE
 }

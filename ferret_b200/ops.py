@@ -181,59 +181,55 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
 
 # ---------------------------------------------------------------- INT4 W4A16
 
-_REPACKED: dict = {}
+class Int4W13Weights:
+    """INT4 W13 weights in the kernel's blob layout (see ferret_int4_repack_w13).
+
+    Built once at load time from the raw compressed-tensors tensors
+    (int32 [E, K/8, N], bf16 scales [E, K/32, N])."""
+
+    def __init__(self, w_raw: torch.Tensor, w_scale: torch.Tensor):
+        _need(w_raw, torch.int32, "w_raw", 3)
+        _need(w_scale, torch.bfloat16, "w_scale", 3)
+        E, K8, N = w_raw.shape
+        K = K8 * 8
+        if tuple(w_scale.shape) != (E, K // 32, N):
+            raise ValueError(f"w_scale must be [{E}, {K // 32}, {N}]")
+        nbytes = lib().ferret_int4_blob_bytes(E, K, N)
+        if nbytes == 0:
+            raise ValueError("K and N must be multiples of 128")
+        self.E, self.K, self.N = E, K, N
+        self.blob = torch.empty(nbytes, dtype=torch.uint8, device=w_raw.device)
+        check(lib().ferret_int4_repack_w13(_ptr(w_raw), _ptr(w_scale), _ptr(self.blob), E, K, N,
+                                           _stream()), "ferret_int4_repack_w13")
 
 
-def int4_repack_w13(w_raw: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Raw compressed-tensors INT4 weights int32 [E, K/8, N] -> the kernel's
-    nibble order (load time, once per weight tensor)."""
-    _need(w_raw, torch.int32, "w_raw", 3)
-    E, K8, N = w_raw.shape
-    if out is None:
-        out = torch.empty_like(w_raw)
-    check(lib().ferret_int4_repack_w13(_ptr(w_raw), _ptr(out), E, K8 * 8, N, _stream()),
-          "ferret_int4_repack_w13")
-    return out
-
-
-def packed_int4_weights(w_raw: torch.Tensor) -> torch.Tensor:
-    """Cached load-time repack, keyed by the tensor's storage, shape and version."""
-    key = (w_raw.data_ptr(), tuple(w_raw.shape), w_raw.device, w_raw._version)
-    hit = _REPACKED.get(key)
-    if hit is None:
-        hit = int4_repack_w13(w_raw)
-        _REPACKED.clear()                 # one weight set at a time is enough here
-        _REPACKED[key] = hit
-    return hit
-
-
-def moe_wna16_w13(hidden: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
-                  topk_ids: torch.Tensor, silu: bool = True, out: torch.Tensor | None = None,
-                  tile: int = 0, perm=None):
+def moe_wna16_w13(hidden: torch.Tensor, weights: Int4W13Weights, topk_ids: torch.Tensor,
+                  silu: bool = True, out: torch.Tensor | None = None, tile: int = 0, perm=None,
+                  workspace: torch.Tensor | None = None):
     """INT4 W4A16 W13: moe_wna16_marlin_gemm + apply_moe_activation(SILU) in one call.
 
-    hidden bf16 [T, K]; w_packed int32 [E, K/8, N] (from int4_repack_w13);
-    w_scale bf16 [E, K/32, N]; topk_ids int32 [T, topk].  Returns bf16
-    [T*topk, N/2 if silu else N] in (token, slot) order; rows of pairs with an
-    invalid expert id are left as allocated (zeros when `out` is None).
+    hidden bf16 [T, K]; weights from Int4W13Weights; topk_ids int32 [T, topk].
+    Returns bf16 [T*topk, N/2 if silu else N] in (token, slot) order; rows of
+    pairs with an invalid expert id are left as allocated (zeros when `out` is None).
     """
     _need(hidden, torch.bfloat16, "hidden", 2)
-    _need(w_packed, torch.int32, "w_packed", 3)
-    _need(w_scale, torch.bfloat16, "w_scale", 3)
     _need(topk_ids, torch.int32, "topk_ids", 2)
     T, K = hidden.shape
-    E, K8, N = w_packed.shape
+    E, N = weights.E, weights.N
     topk = topk_ids.shape[1]
-    if K8 * 8 != K:
-        raise ValueError("hidden and w_packed disagree on K")
+    if K != weights.K:
+        raise ValueError("hidden and weights disagree on K")
     n_out = N // 2 if silu else N
     if out is None:
         out = torch.zeros(T * topk, n_out, dtype=torch.bfloat16, device=hidden.device)
     if perm is None:
         perm = moe_permute(topk_ids, E)
     sorted_rows, offsets, _ = perm
+    ws_bytes = lib().ferret_int4_moe_w13_workspace_size(T, topk, K)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=hidden.device)
     flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
-    check(lib().ferret_int4_moe_w13(_ptr(hidden), _ptr(w_packed), _ptr(w_scale), _ptr(sorted_rows),
-                                    _ptr(offsets), _ptr(out), T, topk, N, K, E, flags, _stream()),
-          "ferret_int4_moe_w13")
+    check(lib().ferret_int4_moe_w13(_ptr(hidden), _ptr(weights.blob), _ptr(sorted_rows),
+                                    _ptr(offsets), _ptr(out), T, topk, N, K, E, flags,
+                                    _ptr(workspace), ws_bytes, _stream()), "ferret_int4_moe_w13")
     return out

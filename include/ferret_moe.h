@@ -159,35 +159,41 @@ FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
     void* out_bf16, const int32_t* m_indices, int M, int N, int K, int E, int flags, void* stream);
 
 /*
- * One-time (load-time) repack of raw compressed-tensors INT4 W13 weights into
- * the layout ferret_int4_moe_w13 reads: same [E, K/8, N] int32 shape, the 8
- * nibbles of each word reordered to K offsets {0,2,4,6,1,3,5,7} so that the
- * kernel turns each (k, k+1) pair into bf16 with one logic op.  The one-time
- * pre-permutation the reference contract allows
+ * One-time (load-time) repack of raw compressed-tensors INT4 W13 weights and
+ * their scales into the blob ferret_int4_moe_w13 reads: for every expert,
+ * 128-row n block and 128-wide K block, 9216 contiguous bytes = 2048 int32
+ * words [k/8][n] (the 8 nibbles of each word reordered to K offsets
+ * {0,2,4,6,1,3,5,7}) followed by the 4 x 128 bf16 group scales [k/32][n].
+ * The one-time pre-permutation the reference contract allows
  * (tasks/kimi-moe-w13-int4-grouped-gemm.yaml:69-71); it replaces the Marlin
  * repack gptq_marlin_moe_repack (baselines/kimi-moe-w13-int4/baseline_marlin.py:80-82).
- * w_raw may equal w_packed (in place).
+ * w_raw int32 [E, K/8, N] (offset-8 nibbles, low nibble first along K),
+ * w_scale_bf16 [E, K/32, N], w_blob: ferret_int4_blob_bytes(E, K, N) bytes.
+ * Limits: K % 128 == 0, N % 128 == 0.
  */
-FERRET_API int ferret_int4_repack_w13(const int32_t* w_raw, int32_t* w_packed, int E, int K, int N,
-                                      void* stream);
+FERRET_API size_t ferret_int4_blob_bytes(int E, int K, int N);
+FERRET_API int ferret_int4_repack_w13(const int32_t* w_raw, const void* w_scale_bf16, void* w_blob,
+                                      int E, int K, int N, void* stream);
 
 /*
  * INT4 W4A16 grouped GEMM for the W13 projection (group-32 symmetric bf16
  * scales, offset-8 nibbles), optional fused SiLU(gate)*up.
  * Replaces: vLLM ops.moe_wna16_marlin_gemm(...) followed by
  *   apply_moe_activation(SILU, ...) (baselines/kimi-moe-w13-int4/baseline_marlin.py:140-168).
- * hidden_bf16  [T, K]; w_packed int32 [E, K/8, N] from ferret_int4_repack_w13;
- * w_scale_bf16 [E, K/32, N]; sorted_rows / expert_offsets from
- * ferret_moe_permute (T*topk flat (token, slot) indices grouped by expert).
- * out_bf16 [T*topk, N] (or [T*topk, N/2] with FERRET_SILU_MUL), row p =
- * (token p/topk, slot p%topk) -- Marlin's output order; rows of dropped pairs
- * are not written.
+ * hidden_bf16 [T, K]; w_blob from ferret_int4_repack_w13; sorted_rows /
+ * expert_offsets from ferret_moe_permute (T*topk flat (token, slot) indices
+ * grouped by expert).  out_bf16 [T*topk, N] (or [T*topk, N/2] with
+ * FERRET_SILU_MUL), row p = (token p/topk, slot p%topk) -- Marlin's output
+ * order; rows of dropped pairs are not written.  The workspace receives the
+ * expert-sorted activation rows: ferret_int4_moe_w13_workspace_size() bytes,
+ * 16-byte aligned.
  * Limits: K % 128 == 0, N % 128 == 0 (N % 256 == 0 with SILU), E <= 1024.
  */
-FERRET_API int ferret_int4_moe_w13(const void* hidden_bf16, const int32_t* w_packed,
-                                   const void* w_scale_bf16, const int32_t* sorted_rows,
-                                   const int32_t* expert_offsets, void* out_bf16, int T, int topk,
-                                   int N, int K, int E, int flags, void* stream);
+FERRET_API size_t ferret_int4_moe_w13_workspace_size(int T, int topk, int K);
+FERRET_API int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
+                                   const int32_t* sorted_rows, const int32_t* expert_offsets,
+                                   void* out_bf16, int T, int topk, int N, int K, int E, int flags,
+                                   void* workspace, size_t ws_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -38,25 +38,39 @@ def inputs(seed, T, E, K, N, topk, hscale=1.0, ids=None):
 
 
 def run(ops, h, rq, sc, ids, silu, tile=0):
-    packed = ops.int4_repack_w13(torch.from_numpy(rq).cuda())
-    out = ops.moe_wna16_w13(torch.from_numpy(h.view(np.int16)).view(torch.bfloat16).cuda(), packed,
-                            torch.from_numpy(sc.view(np.int16)).view(torch.bfloat16).cuda(),
+    wts = ops.Int4W13Weights(torch.from_numpy(rq).cuda(),
+                             torch.from_numpy(sc.view(np.int16)).view(torch.bfloat16).cuda())
+    out = ops.moe_wna16_w13(torch.from_numpy(h.view(np.int16)).view(torch.bfloat16).cuda(), wts,
                             torch.from_numpy(ids).cuda(), silu=silu, tile=tile)
     torch.cuda.synchronize()
     assert ops.last_device_status() == 0
     return O.bf16_to_f32(u16(out))
 
 
-def test_repack_permutes_nibbles(ops):
+def test_repack_blob_layout(ops):
+    """Blob (e, nb, kb) = 2048 nibble-permuted words [k8][n] + bf16 scales [g][n]."""
     rng = np.random.default_rng(0)
-    raw = rng.integers(-2**31, 2**31 - 1, size=(3, 16, 128), dtype=np.int64).astype(np.int32)
-    got = ops.int4_repack_w13(torch.from_numpy(raw).cuda()).cpu().numpy().view(np.uint32)
+    E, K, N = 2, 256, 256
+    raw = rng.integers(-2**31, 2**31 - 1, size=(E, K // 8, N), dtype=np.int64).astype(np.int32)
+    sc = rng.integers(0, 2**16, size=(E, K // 32, N)).astype(np.uint16)
+    wts = ops.Int4W13Weights(torch.from_numpy(raw).cuda(),
+                             torch.from_numpy(sc.view(np.int16)).view(torch.bfloat16).cuda())
+    blob = wts.blob.cpu().numpy()
+    assert blob.size == E * (N // 128) * (K // 128) * 9216
     u = raw.view(np.uint32)
     perm = [0, 2, 4, 6, 1, 3, 5, 7]
-    want = np.zeros_like(u)
-    for slot, k in enumerate(perm):
-        want |= ((u >> np.uint32(4 * k)) & np.uint32(0xF)) << np.uint32(4 * slot)
-    assert np.array_equal(got, want)
+    for e in range(E):
+        for nb in range(N // 128):
+            for kb in range(K // 128):
+                b = ((e * (N // 128) + nb) * (K // 128) + kb) * 9216
+                words = blob[b:b + 8192].view(np.uint32).reshape(16, 128)
+                src = u[e, kb * 16:(kb + 1) * 16, nb * 128:(nb + 1) * 128]
+                want = np.zeros_like(src)
+                for slot, k in enumerate(perm):
+                    want |= ((src >> np.uint32(4 * k)) & np.uint32(0xF)) << np.uint32(4 * slot)
+                assert np.array_equal(words, want)
+                scales = blob[b + 8192:b + 9216].view(np.uint16).reshape(4, 128)
+                assert np.array_equal(scales, sc[e, kb * 4:(kb + 1) * 4, nb * 128:(nb + 1) * 128])
 
 
 @pytest.mark.parametrize("T,E,K,N,topk,silu,tile", [
@@ -113,14 +127,14 @@ def test_int4_kimi_decode_full_size(ops):
     raw, sc = data.int4_weights(cfg.E, cfg.N, cfg.K, device=dev)
     hidden = data.activations(cfg.T, cfg.K)
     ids = data.routing(cfg.T, cfg.E, cfg.topk)
-    packed = ops.int4_repack_w13(raw)
+    packed = ops.Int4W13Weights(raw, sc)
     h_np = u16(hidden)
     flat = ids.numpy().reshape(-1)
     rng = np.random.default_rng(1)
     experts = rng.choice(np.unique(flat), 40, replace=False)
     pairs = np.nonzero(np.isin(flat, experts))[0]
     for silu in (False, True):
-        out = ops.moe_wna16_w13(hidden.to(dev), packed, sc, ids.to(dev), silu=silu)
+        out = ops.moe_wna16_w13(hidden.to(dev), packed, ids.to(dev), silu=silu)
         torch.cuda.synchronize()
         got = O.bf16_to_f32(u16(out))[pairs]
         ref = np.full_like(got, np.nan)
