@@ -20,12 +20,15 @@
 //     a 64-wide K half in the 128-byte-swizzled layout;
 //   * warp 0 (one thread): per K block, one bulk copy of the weight blob (two
 //     with SiLU: gate and up) and two B-tile boxes into an NS-deep ring;
-//   * warps 2-17 (dequant, 512 threads): each thread turns 4 packed words of
-//     one weight row (32 K values, one scale) into four 16-byte bf16 chunks in
-//     the swizzled K-major layout the MMA reads, in a shallower second ring;
-//   * warp 1 (MMA): tcgen05.mma.kind::f16 (bf16 x bf16 -> f32), M = 128 weight
-//     rows, N = NT token rows (swap-AB), K = 16, accumulating the whole K range
-//     in one TMEM buffer per tile (double-buffered across tiles);
+//   * warps 2-17 (dequant, four warpgroups taking 128x128 weight tiles in
+//     turn): the thread of weight row n turns its 16 packed words (128 K
+//     values) into 64 bf16x2 words and stores them with tcgen05.st into TMEM
+//     lane n -- the dequantized A operand never touches shared memory, which
+//     a decode-sized MMA (N = 8 tokens) would otherwise re-read per K step;
+//   * warp 1 (MMA): tcgen05.mma.kind::f16 with A read from TMEM (bf16 x bf16
+//     -> f32), M = 128 weight rows, N = NT token rows (swap-AB), K = 16,
+//     accumulating the whole K range in one TMEM buffer per tile
+//     (double-buffered across tiles);
 //   * warps 18-21 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
 // The dequant arithmetic is exact: nibble pairs become bf16 (128 + n) with one
 // lop3 against the 0x4300 exponent, minus 136 gives n - 8 exactly, and one
@@ -41,13 +44,14 @@ constexpr int kDqWarp0 = 2, kDqWarps = 16, kDqThreads = kDqWarps * 32;
 constexpr int kEpiWarp0 = kDqWarp0 + kDqWarps, kI4EpiThreads = 128;
 constexpr int kI4Threads = (kEpiWarp0 + 4) * 32;   // 22 warps
 constexpr int kI4MaxE = 1024;
-constexpr int kI4MaxStages = 16, kI4MaxDq = 4, kI4MaxAcc = 4;
+constexpr int kDqGroups = kDqWarps / 4;            // dequant warpgroups
+constexpr int kI4MaxStages = 16, kI4MaxQ = 8, kI4MaxAcc = 4;
 constexpr int kRawW = 128 * 16 * 4;    // packed words: 16 k8 rows x 128 n
 constexpr int kRawS = 128 * 4 * 2;     // scales: 4 groups x 128 n bf16
 constexpr int kBlob = kRawW + kRawS;   // 9216 B per 128 x 128 weight block
-constexpr int kDqTile = 128 * 128 * 2; // bf16 128 n x 128 k (two 64-wide atoms)
+constexpr int kQCols = 64;             // TMEM columns of one dequantized 128x128 tile
 
-enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_DQE = 3, I4_DQF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7 };
+enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_QE = 3, I4_QF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7 };
 
 struct Int4Args {
     const uint8_t* blob;          // [E][N/128][K/128] x kBlob
@@ -55,7 +59,7 @@ struct Int4Args {
     const int32_t* offsets;       // [E+1]
     __nv_bfloat16* out;
     int T, topk, N, K, E, R;
-    int stages, dq_stages;
+    int stages;
     DevCtl ctl;
 };
 
@@ -64,22 +68,21 @@ struct I4Cfg {
     static constexpr int kW = PAIR ? 2 : 1;
     static constexpr int kBTile = NT * 256;                     // NT rows x 128 k bf16
     static constexpr int kStage = kW * kBlob + kBTile;          // multiple of 1024
-    static constexpr int kCols = NT * kW;
+    static constexpr int kCols = NT * kW;                       // accumulator columns per tile
     static constexpr int kAcc = 2;
-    static constexpr int kUsed = kAcc * kCols;
-    static constexpr int kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : 256;
+    static constexpr int kAccCols = kAcc * kCols;
+    static constexpr int kQ0 = (512 - kAccCols) / kQCols;       // dequantized-tile slots
+    static constexpr int kQ = kQ0 > kI4MaxQ ? kI4MaxQ : kQ0;
+    static constexpr int kTmemCols = 512;
 };
 
 struct I4Layout {
-    int raw_off, dq_off, mts_off, part_off, bar_off, misc_off, total;
+    int raw_off, mts_off, part_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int dq_bytes,
-                                              int dq_stages, int E) {
+__host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int E) {
     I4Layout L;
     int o = 0;
-    L.dq_off = o;                            // 1024-aligned swizzled tiles first
-    o += dq_bytes * dq_stages;
     L.raw_off = o;                           // B tiles inside need 1024 alignment
     o += stage_bytes * stages;
     L.mts_off = o;
@@ -88,7 +91,7 @@ __host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int d
     o += 4 * (kI4Threads + 1);
     o = (o + 7) & ~7;
     L.bar_off = o;
-    o += 8 * (2 * kI4MaxStages + 2 * kI4MaxDq + 2 * kI4MaxAcc + 1);
+    o += 8 * (2 * kI4MaxStages + 2 * kI4MaxQ + 2 * kI4MaxAcc + 1);
     L.misc_off = o;
     o += 16;
     L.total = o;
@@ -150,34 +153,34 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int N = args.N, K = args.K, E = args.E, NS = args.stages, ND = args.dq_stages;
+    const int N = args.N, K = args.K, E = args.E, NS = args.stages;
+    constexpr int NQ = C::kQ;
     const int nk = K >> 7;
     const int nbc = PAIR ? (N >> 8) : (N >> 7);
-    const I4Layout L = i4_layout(C::kStage, NS, C::kW * kDqTile, ND, E);
+    const I4Layout L = i4_layout(C::kStage, NS, E);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
     int* part = reinterpret_cast<int*>(smem + L.part_off);
     const uint32_t bar0 = smem_addr(smem + L.bar_off);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kI4MaxStages + s); };
-    auto dqf_bar = [&](int d) { return bar0 + 8u * (2 * kI4MaxStages + d); };
-    auto dqe_bar = [&](int d) { return bar0 + 8u * (2 * kI4MaxStages + kI4MaxDq + d); };
-    auto tf_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + a); };
-    auto te_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + kI4MaxAcc + a); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxDq + 2 * kI4MaxAcc);
+    auto qf_bar = [&](int q) { return bar0 + 8u * (2 * kI4MaxStages + q); };
+    auto qe_bar = [&](int q) { return bar0 + 8u * (2 * kI4MaxStages + kI4MaxQ + q); };
+    auto tf_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + a); };
+    auto te_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + kI4MaxAcc + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + 2 * kI4MaxAcc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
     uint8_t* raw = smem + L.raw_off;
-    uint8_t* dq = smem + L.dq_off;
-    const uint32_t raw_base = smem_addr(raw), dq_base = smem_addr(dq);
+    const uint32_t raw_base = smem_addr(raw);
 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
-        for (int d = 0; d < ND; ++d) {
-            mbar_init(dqf_bar(d), kDqWarps);
-            mbar_init(dqe_bar(d), 1);
+        for (int q = 0; q < NQ; ++q) {
+            mbar_init(qf_bar(q), 4);             // one arrival per warp of a dequant group
+            mbar_init(qe_bar(q), 1);
         }
         for (int a = 0; a < C::kAcc; ++a) {
             mbar_init(tf_bar(a), 1);
@@ -205,6 +208,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const uint32_t q_base = tmem_base + C::kAccCols;          // dequantized-tile slots
     const int total = mt_start[E] * nbc;
     const size_t blob_nb = (size_t)(K >> 7) * kBlob;          // bytes per (e, n-block)
 
@@ -245,38 +249,47 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         // ================= MMA issuer =================
         if (elect_one()) {
             constexpr uint32_t idesc = make_idesc(128, NT, 1, 1);
-            RingPos rs, rd, ra;
+            RingPos rs, rq, ra;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ra.advance(C::kAcc)) {
                 const int a = ra.slot;
                 if (!mbar_wait(te_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, I4_TE)) break;
                 const uint32_t d_acc = tmem_base + a * C::kCols;
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), rd.advance(ND)) {
-                    const int s = rs.slot, d = rd.slot;
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS)) {
+                    const int s = rs.slot;
+                    RingPos qw[C::kW];
+                    qw[0] = rq;
+                    rq.advance(NQ);
+                    if (PAIR) {
+                        qw[C::kW - 1] = rq;
+                        rq.advance(NQ);
+                    }
                     // the B tile comes straight from the copy engine; the
-                    // dequantized A tile from the dequant warps
-                    if (!mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL) ||
-                        !mbar_wait(dqf_bar(d), rd.phase, abort_flag, args.ctl, I4_DQF)) {
+                    // dequantized A tiles from the dequant warpgroups
+                    bool ready = mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL);
+#pragma unroll
+                    for (int w = 0; w < C::kW; ++w)
+                        ready = ready && mbar_wait(qf_bar(qw[w].slot), qw[w].phase, abort_flag,
+                                                   args.ctl, I4_QF);
+                    if (!ready) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t bt = raw_base + s * C::kStage + C::kW * kBlob;
-                    const uint32_t wt = dq_base + d * (C::kW * kDqTile);
 #pragma unroll
-                    for (int ac = 0; ac < 2; ++ac) {
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint32_t acc = (kb | ks) ? 1u : 0u;
+                        const uint64_t bdesc =
+                            sdesc_k_sw128(bt + (ks >> 2) * NT * 128 + (ks & 3) * 32);
 #pragma unroll
-                        for (int ks = 0; ks < 4; ++ks) {
-                            const uint32_t acc = (kb | ac | ks) ? 1u : 0u;
-                            const uint64_t bdesc = sdesc_k_sw128(bt + ac * NT * 128 + ks * 32);
-                            mma_f16(d_acc, sdesc_k_sw128(wt + ac * 16384 + ks * 32), bdesc, idesc, acc);
-                            if (PAIR)
-                                mma_f16(d_acc + NT, sdesc_k_sw128(wt + kDqTile + ac * 16384 + ks * 32),
-                                        bdesc, idesc, acc);
-                        }
+                        for (int w = 0; w < C::kW; ++w)
+                            mma_f16_tmem_a(d_acc + w * NT, q_base + qw[w].slot * kQCols + ks * 8, bdesc,
+                                           idesc, acc);
                     }
                     tc_commit(empty_bar(s));
-                    tc_commit(dqe_bar(d));
+#pragma unroll
+                    for (int w = 0; w < C::kW; ++w) tc_commit(qe_bar(qw[w].slot));
                 }
                 if (!ok) break;
                 tc_commit(tf_bar(a));
@@ -286,53 +299,52 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         }
     } else if (warp < kEpiWarp0) {
         // ================= dequant =================
-        const int dt = tid - kDqWarp0 * 32;
-        constexpr int kUnits = 512 / kDqThreads;   // (scale group, weight row) units per thread
-        RingPos rs, rd;
+        // group g takes the weight tiles g, g+4, g+8, ... in issue order; the
+        // thread of TMEM lane n (its warp's lane quarter) owns weight row n
+        const int g = (warp - kDqWarp0) >> 2;
+        const int n = ((warp & 3) << 5) + lane;
+        const uint32_t lane_addr = (uint32_t)((warp & 3) << 5) << 16;
+        RingPos rs, rq;
+        int job = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            for (int kb = 0; kb < nk; ++kb, rs.advance(NS), rd.advance(ND)) {
-                const int s = rs.slot, d = rd.slot;
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, I4_FULL) &&
-                                    mbar_wait(dqe_bar(d), rd.phase ^ 1u, abort_flag, args.ctl, I4_DQE));
-                if (!ok) break;
-                const uint8_t* st = raw + s * C::kStage;
-                uint8_t* out_tile = dq + d * (C::kW * kDqTile);
-                // all shared loads first (they cannot be reordered past the
-                // stores below), then convert and store
-                uint32_t wv[C::kW][kUnits][4], sv[C::kW][kUnits];
+            for (int kb = 0; kb < nk && ok; ++kb, rs.advance(NS)) {
 #pragma unroll
-                for (int w = 0; w < C::kW; ++w) {
-                    const uint32_t* words = reinterpret_cast<const uint32_t*>(st + w * kBlob);
-                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + w * kBlob + kRawW);
+                for (int w = 0; w < C::kW; ++w, ++job, rq.advance(NQ)) {
+                    if ((job & (kDqGroups - 1)) != g) continue;
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(full_bar(rs.slot), rs.phase, abort_flag, args.ctl, I4_FULL) &&
+                                        mbar_wait(qe_bar(rq.slot), rq.phase ^ 1u, abort_flag, args.ctl,
+                                                  I4_QE));
+                    if (!ok) break;
+                    const uint8_t* blob = raw + rs.slot * C::kStage + w * kBlob;
+                    const uint32_t* words = reinterpret_cast<const uint32_t*>(blob);
+                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(blob + kRawW);
+                    const uint32_t col = q_base + rq.slot * kQCols + lane_addr;
 #pragma unroll
-                    for (int ui = 0; ui < kUnits; ++ui) {
-                        const int u = dt + ui * kDqThreads, g = u >> 7, n = u & 127;
-                        sv[w][ui] = sc[g * 128 + n];
+                    for (int h = 0; h < 2; ++h) {          // K halves: 64 values, 32 columns
+                        uint32_t wv[8];
+                        uint32_t s0 = sc[(2 * h) * 128 + n], s1 = sc[(2 * h + 1) * 128 + n];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) wv[w][ui][q] = words[(g * 4 + q) * 128 + n];
-                    }
-                }
+                        for (int i = 0; i < 8; ++i) wv[i] = words[(8 * h + i) * 128 + n];
+                        s0 |= s0 << 16;
+                        s1 |= s1 << 16;
+                        uint32_t r[32];
 #pragma unroll
-                for (int w = 0; w < C::kW; ++w) {
-#pragma unroll
-                    for (int ui = 0; ui < kUnits; ++ui) {
-                        const int u = dt + ui * kDqThreads, g = u >> 7, n = u & 127;
-                        uint8_t* tile = out_tile + w * kDqTile + n * 128;
-                        const uint32_t s2 = sv[w][ui] | (sv[w][ui] << 16);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const int k8 = g * 4 + q;                    // 0..15
-                            const uint4 v = dequant_word(wv[w][ui][q], s2);
-                            const int ac = k8 >> 3, c = k8 & 7;
-                            *reinterpret_cast<uint4*>(tile + ac * 16384 + ((c ^ (n & 7)) << 4)) = v;
+                        for (int i = 0; i < 8; ++i) {
+                            const uint4 v = dequant_word(wv[i], i < 4 ? s0 : s1);
+                            r[4 * i + 0] = v.x;
+                            r[4 * i + 1] = v.y;
+                            r[4 * i + 2] = v.z;
+                            r[4 * i + 3] = v.w;
                         }
+                        tmem_st32(col + h * 32, r);
                     }
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(qf_bar(rq.slot));
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(dqf_bar(d));
             }
         }
     } else {
@@ -453,13 +465,12 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
     int rc = make_tmap_2d(&tm_a, a_sorted, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, (uint64_t)K * 2,
                           64, NT, true);
     if (rc != FERRET_OK) return rc;
+    static_assert(C::kQ >= C::kW * 2, "too few TMEM tile slots");
     const int budget = info->max_smem_optin - 1024;
-    const int dq_bytes = C::kW * kDqTile;
-    const int nd = PAIR ? 2 : 4;
-    const I4Layout l0 = i4_layout(C::kStage, 0, dq_bytes, nd, E);
+    const I4Layout l0 = i4_layout(C::kStage, 0, E);
     const int stages = std::min(kI4MaxStages, (budget - l0.total) / C::kStage);
     if (stages < 2) return FERRET_ERR_SHAPE;
-    const I4Layout L = i4_layout(C::kStage, stages, dq_bytes, nd, E);
+    const I4Layout L = i4_layout(C::kStage, stages, E);
     const int smem = L.total + 1024;
     auto kern = int4_w13_grouped_kernel<NT, PAIR>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
@@ -478,7 +489,6 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
     a.E = E;
     a.R = R;
     a.stages = stages;
-    a.dq_stages = nd;
     a.ctl = make_ctl(info);
     kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_a, a);
     return launch_status();
