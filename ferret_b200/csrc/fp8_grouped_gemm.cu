@@ -448,6 +448,315 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Prefill-shaped kernel: tokens on the MMA M axis.
+//
+// When experts carry many tokens the swap-AB orientation wastes issue slots:
+// its per-column (per-token) scales cost a multiply per accumulator element.
+// Here a CTA tile is 128 token rows (MMA M) x 256 weight rows (MMA N: two
+// 128-row weight blocks -- consecutive ones, or gate block j and up block
+// N/256 + j with SiLU), 128-wide K blocks (48 KB stages, TMA, 128-byte
+// swizzle).  tcgen05.mma kind::f8f6f4 M=128 N=256 K=32 writes each K block's
+// partial into one of two 256-column TMEM buffers; 8 epilogue warps promote
+// it: thread (row r, column half h) owns 64 columns of each weight block and
+// needs just two scale products per K block (a_scale[r] * w_scale[block]),
+// then 128 FMAs.  SiLU pairs land in the same thread (gate column c and up
+// column 128 + c), so the fused epilogue needs no exchange.
+// ---------------------------------------------------------------------------
+constexpr int kPfThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kPfEpi = 256;
+constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
+constexpr int kPfMaxStages = 6;
+
+struct PfLayout {
+    int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
+};
+
+__host__ __device__ inline PfLayout pf_layout(int stages, int E) {
+    PfLayout L;
+    int o = 0;
+    L.stages_off = o;
+    o += kPfStage * stages;
+    L.segs_off = o;
+    o += 4 * E;
+    L.segc_off = o;
+    o += 4 * E;
+    L.mts_off = o;
+    o += 4 * (E + 1);
+    L.part_off = o;
+    o += 4 * (kPfThreads + 1);
+    o = (o + 7) & ~7;
+    L.bar_off = o;
+    o += 8 * (2 * kPfMaxStages + 2 * 2 + 2);
+    L.misc_off = o;
+    o += 16;
+    L.total = o;
+    return L;
+}
+
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;                        // 256-row weight tiles
+    const PfLayout L = pf_layout(NS, E);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
+    const uint32_t epi_bar = drain_bar + 8u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kPfEpi);
+        }
+        mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kPfEpi);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        seg_s[e] = s;
+        seg_c[e] = c;
+        mt_start[e] = (c + 127) >> 7;
+    }
+    if (seg_bad) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
+            const uint64_t pol_a = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
+                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = stage_base + s * kPfStage;
+                    mbar_expect_tx(full_bar(s), kPfStage);
+                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
+                }
+            }
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (elect_one()) {
+            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
+                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPfStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
+                                   idesc, ks > 0);
+                    tc_commit(empty_bar(s));
+                    tc_commit(tfull_bar(a));
+                }
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else {
+        // ================= epilogue: promotion + store =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        RingPos ra;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int e, row0, rows, nb;
+            decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const bool live = r < rows;
+            const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                       args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(ra.slot));
+            }
+            if (!ok) break;
+            if (live) {
+                __nv_bfloat16* o = args.out + (size_t)(row0 + r) * ldo;
+                if (PAIR) {
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 pk;
+                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                        }
+                        dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+template <bool PAIR>
+int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                       int N, int K, int E, cudaStream_t stream) {
+    CUtensorMap tm_w, tm_a;
+    int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
+                          128, true);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
+    if (rc != FERRET_OK) return rc;
+    const int budget = info->max_smem_optin - 1024;
+    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E).total) / kPfStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const int smem = pf_layout(stages, E).total + 1024;
+    auto kern = fp8_w13_prefill_kernel<PAIR>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    GemmArgs g;
+    g.a_scale = a_scale;
+    g.w_scale = w_scale;
+    g.seg = seg;
+    g.seg_pairs = seg_pairs;
+    g.out = static_cast<__nv_bfloat16*>(out);
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.E = E;
+    g.stages = stages;
+    g.ctl = make_ctl(info);
+    kern<<<info->num_sms, kPfThreads, smem, stream>>>(tm_w, tm_a, g);
+    return launch_status();
+}
+
 int pick_tile(int M, int E, int flags, bool pair) {
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
     if (nt == 0) {
@@ -456,6 +765,14 @@ int pick_tile(int M, int E, int flags, bool pair) {
     }
     if (pair && nt > 64) nt = 64;
     return nt;
+}
+
+// 128-token tiles (requested, or experts averaging more than 48 rows) run on
+// the prefill kernel when the weight tiles (256 rows) divide N.
+bool use_prefill(int M, int E, int flags, int N) {
+    int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
+    if (nt == 0) nt = ((M + E - 1) / std::max(E, 1)) > 48 ? 128 : 0;
+    return nt == 128 && N % 256 == 0;
 }
 
 }  // namespace
@@ -502,6 +819,12 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
         seg_pairs = 1;
     }
 
+    // many tokens per expert: the prefill kernel (tokens on MMA M, 256 weight rows on N)
+    if (use_prefill(M, E, flags, N))
+        return pair ? launch_fp8_prefill<true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg,
+                                               seg_pairs, M, N, K, E, s)
+                    : launch_fp8_prefill<false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg,
+                                                seg_pairs, M, N, K, E, s);
     const int nt = pick_tile(M, E, flags, pair);
 #define FERRET_FP8_CASE(NT_)                                                                     \
     case NT_:                                                                                    \

@@ -157,6 +157,11 @@ CASES = [
     ([1] * 12, 256, 1024, 0, False, 0),
     ([8, 8, 8, 8], 256, 128, 5, False, 16),     # DeepGEMM-style padding rows
     ([8, 8, 8, 8], 256, 128, 5, True, 0),
+    # the prefill kernel (128-token tiles on MMA M, 256 weight rows on MMA N)
+    ([300, 129, 2, 0, 77], 512, 384, 0, False, 128),
+    ([300, 129, 2, 0, 77], 512, 384, 0, True, 128),
+    ([40, 40, 40, 40], 256, 128, 5, False, 128),
+    ([1000], 256, 256, 0, True, 128),
 ]
 
 
@@ -276,3 +281,34 @@ def test_ep_single_rank_matches_w13_path(ops):
         got = ep.forward(hidden, ids)
         torch.cuda.synchronize()
         assert torch.equal(got.view(torch.int16), tk.view(torch.int16))
+
+
+def test_w13_path_dsv3_prefill_full_size(ops):
+    """BASELINE config 3 (E=256, top-8 Zipf(1.1), 8192 tokens) at full size, plain
+    and fused SiLU: every row of 6 sampled experts (the largest among them)
+    against the fp32 oracle."""
+    from ferret_b200 import data
+    cfg = data.CONFIGS["dsv3_prefill"]
+    dev = torch.device("cuda")
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, "zipf")
+    r_rows, r_offs, _ = O.moe_permute(ids.numpy(), cfg.E)
+    counts = np.diff(r_offs)
+    experts = [int(np.argmax(counts))] + list(np.random.default_rng(2).choice(
+        np.nonzero(counts)[0], 5, replace=False))
+    for silu in (False, True):
+        out, rows, offs = ops.fp8_moe_w13(hidden.cuda(), ids.cuda(), W, Ws, silu=silu)
+        torch.cuda.synchronize()
+        assert np.array_equal(offs.cpu().numpy(), r_offs)
+        got = O.bf16_to_f32(u16(out))
+        qd, sd = u8(ops.per_token_cast_to_fp8(hidden.cuda(), rows, cfg.topk)[0]), None
+        q, s = ops.per_token_cast_to_fp8(hidden.cuda(), rows, cfg.topk)
+        q, s = u8(q), s.cpu().numpy()
+        for e in experts:
+            r0, r1 = r_offs[e], r_offs[e + 1]
+            ref = O.fp8_grouped_gemm_fast(q[r0:r1], s[r0:r1], u8(W[e:e + 1]), Ws[e:e + 1].cpu().numpy(),
+                                          np.zeros(r1 - r0, np.int32), silu=silu)
+            err = O.rel_err(got[r0:r1], ref)
+            assert err["nan"] == 0 and err["max_rel"] < TOL, (silu, int(e), err)
+    assert ops.last_device_status() == 0
