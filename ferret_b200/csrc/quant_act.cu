@@ -10,25 +10,36 @@
 // IEEE round-to-nearest (no fast-math), so the result is bit-identical to the
 // CPU restatement.
 //
-// HBM-bound: one warp per 128-element block, 8 bytes per lane in, 4 out.
+// HBM-bound: a warp quantizes 4 blocks of a row per task, 16 bytes per lane in.
 #include "capi_internal.h"
 
 namespace ferret {
 namespace {
 
 constexpr int kQuantThreads = 256;
+constexpr int kBlocksPerTask = 4;     // 128-element blocks one warp handles per task
 
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// A warp task is (row, 4 consecutive 128-element blocks).  Each half-warp
+// covers one block with 16-byte loads; both loads of a lane are issued before
+// either is used, so 1 KB per warp is in flight (the kernel is bound by the
+// latency of the gathered row reads, not by HBM, at decode sizes).
 __global__ void __launch_bounds__(kQuantThreads)
     quant_act_kernel(const __nv_bfloat16* __restrict__ x, int x_rows,
                      const int32_t* __restrict__ gather, int gather_div, int R, int K,
                      uint8_t* __restrict__ q, float* __restrict__ scale, DevCtl ctl) {
     const int nk = K >> 7;
-    const long long tasks = (long long)R * nk;
+    const int tasks_per_row = (nk + kBlocksPerTask - 1) / kBlocksPerTask;
+    const long long tasks = (long long)R * tasks_per_row;
     const int lane = threadIdx.x & 31;
+    const int half = lane >> 4, hl = lane & 15;
     const long long warps = (long long)gridDim.x * (kQuantThreads / 32);
     for (long long task = (long long)blockIdx.x * (kQuantThreads / 32) + (threadIdx.x >> 5);
          task < tasks; task += warps) {
-        const int r = (int)(task / nk), b = (int)(task % nk);
+        const int r = (int)(task / tasks_per_row);
+        const int b0 = (int)(task - (long long)r * tasks_per_row) * kBlocksPerTask;
         long long src = r;
         if (gather) {
             const int g = gather[r];
@@ -38,31 +49,52 @@ __global__ void __launch_bounds__(kQuantThreads)
                 src = -1;
             }
         }
-        uint8_t* qdst = q + (long long)r * K + b * 128 + lane * 4;
-        if (src < 0) {
-            *reinterpret_cast<uint32_t*>(qdst) = 0u;
-            if (lane == 0) scale[(long long)r * nk + b] = 0.0f;
-            continue;
-        }
-        const uint2 raw =
-            *reinterpret_cast<const uint2*>(x + src * K + b * 128 + lane * 4);
-        const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        const float v0 = __low2float(p0), v1 = __high2float(p0);
-        const float v2 = __low2float(p1), v3 = __high2float(p1);
-        float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+        uint4 raw[kBlocksPerTask / 2];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        amax = fmaxf(amax, 1e-4f);
-        // `448.0 / amax` in the published torch code is reciprocal-then-multiply
-        const float f = __fmul_rn(__frcp_rn(amax), 448.0f);
-        const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-            make_float2(__fmul_rn(v0, f), __fmul_rn(v1, f)), __NV_SATFINITE, __NV_E4M3);
-        const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-            make_float2(__fmul_rn(v2, f), __fmul_rn(v3, f)), __NV_SATFINITE, __NV_E4M3);
-        *reinterpret_cast<uint32_t*>(qdst) = (uint32_t)lo | ((uint32_t)hi << 16);
-        if (lane == 0) scale[(long long)r * nk + b] = __fdiv_rn(amax, 448.0f);
+        for (int i = 0; i < kBlocksPerTask / 2; ++i) {
+            const int b = b0 + 2 * i + half;
+            raw[i] = (src >= 0 && b < nk)
+                         ? *reinterpret_cast<const uint4*>(x + src * K + b * 128 + hl * 8)
+                         : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < kBlocksPerTask / 2; ++i) {
+            const int b = b0 + 2 * i + half;
+            const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[2 * j] = bf16_lo(w[j]);
+                v[2 * j + 1] = bf16_hi(w[j]);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1)      // within the 16-lane half
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            if (b >= nk) continue;
+            amax = fmaxf(amax, 1e-4f);
+            // `448.0 / amax` in the published torch code is reciprocal-then-multiply
+            const float f = __fmul_rn(__frcp_rn(amax), 448.0f);
+            uint32_t packed[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+                    make_float2(__fmul_rn(v[4 * j], f), __fmul_rn(v[4 * j + 1], f)), __NV_SATFINITE,
+                    __NV_E4M3);
+                const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+                    make_float2(__fmul_rn(v[4 * j + 2], f), __fmul_rn(v[4 * j + 3], f)),
+                    __NV_SATFINITE, __NV_E4M3);
+                packed[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+            }
+            uint8_t* qdst = q + (long long)r * K + b * 128 + hl * 8;
+            if (src < 0) {
+                packed[0] = packed[1] = 0u;
+            }
+            *reinterpret_cast<uint2*>(qdst) = make_uint2(packed[0], packed[1]);
+            if (hl == 0) scale[(long long)r * nk + b] = src < 0 ? 0.0f : __fdiv_rn(amax, 448.0f);
+        }
     }
 }
 
@@ -79,15 +111,15 @@ extern "C" int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows,
     if (R == 0) return FERRET_OK;
     if (!x_bf16 || !a_fp8 || !a_scale) return FERRET_ERR_NULL;
     if (gather_rows && gather_div <= 0) return FERRET_ERR_SHAPE;
-    if ((reinterpret_cast<uintptr_t>(x_bf16) & 7u) || (reinterpret_cast<uintptr_t>(a_fp8) & 3u) ||
+    if ((reinterpret_cast<uintptr_t>(x_bf16) & 15u) || (reinterpret_cast<uintptr_t>(a_fp8) & 7u) ||
         (reinterpret_cast<uintptr_t>(a_scale) & 3u))
         return FERRET_ERR_ALIGN;
     DeviceInfo* info = nullptr;
     int rc = current_device(&info);
     if (rc != FERRET_OK) return rc;
-    const long long tasks = (long long)R * (K / 128);
+    const long long tasks = (long long)R * ((K / 128 + kBlocksPerTask - 1) / kBlocksPerTask);
     const long long want = (tasks + (kQuantThreads / 32) - 1) / (kQuantThreads / 32);
-    const int grid = (int)(want < (long long)info->num_sms * 8 ? want : (long long)info->num_sms * 8);
+    const int grid = (int)(want < (long long)info->num_sms * 16 ? want : (long long)info->num_sms * 16);
     quant_act_kernel<<<grid, kQuantThreads, 0, as_stream(stream)>>>(
         static_cast<const __nv_bfloat16*>(x_bf16), x_rows, gather_rows, gather_div, R, K,
         static_cast<uint8_t*>(a_fp8), a_scale, make_ctl(info));

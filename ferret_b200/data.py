@@ -57,6 +57,9 @@ CONFIGS = {
     # reference's own per-rank decode shape (tasks/fp8-group-gemm-dsv3-decode.yaml:14),
     # also the small case for ncu captures (0.94 GB of weights > L2)
     "dsv3_decode_rank": W13Config("dsv3_decode_rank", E=32, topk=8, T=16, K=7168, N=4096),
+    # small FP8 prefill case for ncu captures (32 experts, 0.94 GB of weights)
+    "dsv3_prefill_small": W13Config("dsv3_prefill_small", E=32, topk=8, T=2048, K=7168, N=4096,
+                                    routing="zipf"),
     # small INT4 case for ncu captures (~35 active experts, ~0.6 GB of weights > L2)
     "kimi_int4_small": W13Config("kimi_int4_small", E=48, topk=8, T=8, K=7168, N=4096,
                                  quant="int4"),
