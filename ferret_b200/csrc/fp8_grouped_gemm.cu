@@ -495,7 +495,7 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E) {
 }
 
 template <bool PAIR>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 64K
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
@@ -648,29 +648,56 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 acc0[j] = 0.0f;
                 acc1[j] = 0.0f;
             }
+            // scales are prefetched 4 K blocks ahead so their load latency
+            // never sits between a TMEM buffer becoming full and its release
+            constexpr int kPre = 4;
+            float na[kPre], n0[kPre], n1[kPre];
+#pragma unroll
+            for (int j = 0; j < kPre; ++j) {
+                const bool in = j < nk;
+                na[j] = (in && live) ? __ldg(as_row + j) : 0.0f;
+                n0[j] = in ? __ldg(ws0 + j) : 0.0f;
+                n1[j] = in ? __ldg(ws1 + j) : 0.0f;
+            }
             bool ok = true;
-            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
-                const float sa = live ? __ldg(as_row + kb) : 0.0f;
-                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
-                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
-                                                       args.ctl, SITE_TFULL));
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+            for (int kc = 0; kc < nk && ok; kc += kPre) {
+                float s0v[kPre], s1v[kPre];
 #pragma unroll
-                for (int c = 0; c < 64; c += 16) {
-                    float v[16], u[16];
-                    tmem_ld16(tb + c, v);
-                    tmem_ld16(tb + 128 + c, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
-                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
-                    }
+                for (int j = 0; j < kPre; ++j) {
+                    s0v[j] = na[j] * n0[j];
+                    s1v[j] = na[j] * n1[j];
+                    const int kn = kc + kPre + j;
+                    const bool in = kn < nk;
+                    na[j] = (in && live) ? __ldg(as_row + kn) : 0.0f;
+                    n0[j] = in ? __ldg(ws0 + kn) : 0.0f;
+                    n1[j] = in ? __ldg(ws1 + kn) : 0.0f;
                 }
-                tc_fence_before();
-                mbar_arrive(tempty_bar(ra.slot));
+#pragma unroll
+                for (int j = 0; j < kPre; ++j) {
+                    if (kc + j >= nk) break;
+                    ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                           args.ctl, SITE_TFULL));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                    for (int c = 0; c < 64; c += 16) {
+                        float v[16], u[16];
+                        tmem_ld16(tb + c, v);
+                        tmem_ld16(tb + 128 + c, u);
+                        tmem_ld_wait();
+                        if (c == 48) {                 // all reads of this buffer done
+                            tc_fence_before();
+                            mbar_arrive(tempty_bar(ra.slot));
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            acc0[c + i] = fmaf(v[i], s0v[j], acc0[c + i]);
+                            acc1[c + i] = fmaf(u[i], s1v[j], acc1[c + i]);
+                        }
+                    }
+                    ra.advance(2);
+                }
             }
             if (!ok) break;
             if (live) {
