@@ -465,6 +465,7 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
 // ---------------------------------------------------------------------------
 constexpr int kPfThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kPfEpi = 256;
+constexpr int kPfCols = 64;              // columns of each 128-column half per epilogue thread
 constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
 constexpr int kPfMaxStages = 6;
 
@@ -495,7 +496,7 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E) {
 }
 
 template <bool PAIR>
-__global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 64K
+__global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
@@ -627,7 +628,7 @@ __global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 
         }
     } else {
         // ================= epilogue: promotion + store =================
-        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int h = (warp - 2) >> 2;           // columns [64h, 64h+64) of each block
         const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
@@ -642,9 +643,9 @@ __global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 
             const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
             const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
             const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
-            float acc0[64], acc1[64];
+            float acc0[kPfCols], acc1[kPfCols];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
+            for (int j = 0; j < kPfCols; ++j) {
                 acc0[j] = 0.0f;
                 acc1[j] = 0.0f;
             }
@@ -661,39 +662,37 @@ __global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 
             }
             bool ok = true;
             for (int kc = 0; kc < nk && ok; kc += kPre) {
-                float s0v[kPre], s1v[kPre];
-#pragma unroll
-                for (int j = 0; j < kPre; ++j) {
-                    s0v[j] = na[j] * n0[j];
-                    s1v[j] = na[j] * n1[j];
-                    const int kn = kc + kPre + j;
-                    const bool in = kn < nk;
-                    na[j] = (in && live) ? __ldg(as_row + kn) : 0.0f;
-                    n0[j] = in ? __ldg(ws0 + kn) : 0.0f;
-                    n1[j] = in ? __ldg(ws1 + kn) : 0.0f;
-                }
 #pragma unroll
                 for (int j = 0; j < kPre; ++j) {
                     if (kc + j >= nk) break;
+                    // this K block's scales; the slot then prefetches kPre blocks ahead
+                    const float s0 = na[j] * n0[j], s1 = na[j] * n1[j];
+                    {
+                        const int kn = kc + kPre + j;
+                        const bool in = kn < nk;
+                        na[j] = (in && live) ? __ldg(as_row + kn) : 0.0f;
+                        n0[j] = in ? __ldg(ws0 + kn) : 0.0f;
+                        n1[j] = in ? __ldg(ws1 + kn) : 0.0f;
+                    }
                     ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
                                                            args.ctl, SITE_TFULL));
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+                    const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * kPfCols;
 #pragma unroll
-                    for (int c = 0; c < 64; c += 16) {
-                        float v[16], u[16];
-                        tmem_ld16(tb + c, v);
-                        tmem_ld16(tb + 128 + c, u);
+                    for (int c = 0; c < kPfCols; c += 8) {
+                        float v[8], u[8];
+                        tmem_ld8(tb + c, v);
+                        tmem_ld8(tb + 128 + c, u);
                         tmem_ld_wait();
-                        if (c == 48) {                 // all reads of this buffer done
+                        if (c == kPfCols - 8) {       // all reads of this buffer done
                             tc_fence_before();
                             mbar_arrive(tempty_bar(ra.slot));
                         }
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            acc0[c + i] = fmaf(v[i], s0v[j], acc0[c + i]);
-                            acc1[c + i] = fmaf(u[i], s1v[j], acc1[c + i]);
+                        for (int i = 0; i < 8; ++i) {
+                            acc0[c + i] = fmaf(v[i], s0, acc0[c + i]);
+                            acc1[c + i] = fmaf(u[i], s1, acc1[c + i]);
                         }
                     }
                     ra.advance(2);
@@ -703,9 +702,9 @@ __global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 
             if (live) {
                 __nv_bfloat16* o = args.out + (size_t)(row0 + r) * ldo;
                 if (PAIR) {
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * kPfCols);
 #pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
+                    for (int c = 0; c < kPfCols; c += 8) {
                         uint4 pk;
                         uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
@@ -718,10 +717,10 @@ __global__ void __maxnreg__(200)    // 320 threads x 200 registers fit the SM's 
                         dst[c >> 3] = pk;
                     }
                 } else {
-                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
-                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * kPfCols);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * kPfCols);
 #pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
+                    for (int c = 0; c < kPfCols; c += 8) {
                         uint4 p0, p1;
                         uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
                         uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
