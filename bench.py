@@ -291,7 +291,7 @@ def run_single(args, cfg):
     e_ms = sum(e2e_ms) / len(e2e_ms)
     pk = peaks()
     # the library runs the prefill kernel when experts average more than 48 rows
-    prefill = (cfg.R + cfg.E - 1) // cfg.E > 48
+    prefill = (cfg.R + cfg.E - 1) // cfg.E > 48 and cfg.N % 256 == 0
     rl = roofline(byts, flops, g_ms, pk, "fp8_w13_prefill_kernel" if prefill else "fp8_w13_grouped_kernel")
     res = {
         "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",

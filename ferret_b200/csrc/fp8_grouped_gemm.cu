@@ -453,22 +453,20 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
 //
 // When experts carry many tokens the swap-AB orientation wastes issue slots:
 // its per-column (per-token) scales cost a multiply per accumulator element.
-// Here a CTA tile is 128 token rows (MMA M) x 128 weight rows (MMA N: one
-// 128-row weight block, or with SiLU the 64-row halves gate[64j, 64j+64) and
-// up[N/2 + 64j, ...)), 128-wide K blocks (32 KB stages, TMA, 128-byte
-// swizzle).  tcgen05.mma kind::f8f6f4 M=128 N=128 K=32 writes each K block's
-// partial into one of four 128-column TMEM buffers, so the MMA can run three
-// K blocks ahead of the promotion.  8 epilogue warps promote: thread (row r,
-// column half h) owns 64 accumulator columns, issues all its TMEM loads of a
-// K block before one wait, and applies a_scale[r] * w_scale[block] (one or,
-// with SiLU, two products per K block) with 64 FMAs.  SiLU pairs (gate column
-// c, up column 64 + c) land in the same thread.
+// Here a CTA tile is 128 token rows (MMA M) x 256 weight rows (MMA N: two
+// 128-row weight blocks -- consecutive ones, or gate block j and up block
+// N/256 + j with SiLU), 128-wide K blocks (48 KB stages, TMA, 128-byte
+// swizzle).  tcgen05.mma kind::f8f6f4 M=128 N=256 K=32 writes each K block's
+// partial into one of two 256-column TMEM buffers; 8 epilogue warps promote
+// it: thread (row r, column half h) owns 64 columns of each weight block and
+// needs just two scale products per K block (a_scale[r] * w_scale[block]),
+// then 128 FMAs.  SiLU pairs land in the same thread (gate column c and up
+// column 128 + c), so the fused epilogue needs no exchange.
 // ---------------------------------------------------------------------------
 constexpr int kPfThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kPfEpi = 256;
-constexpr int kPfBufs = 4;               // TMEM partial buffers of 128 columns
-constexpr int kPfStage = 128 * 128 + 128 * 128;   // A 16 KB + B 16 KB
-constexpr int kPfMaxStages = 8;
+constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
+constexpr int kPfMaxStages = 6;
 
 struct PfLayout {
     int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
@@ -489,7 +487,7 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E) {
     o += 4 * (kPfThreads + 1);
     o = (o + 7) & ~7;
     L.bar_off = o;
-    o += 8 * (2 * kPfMaxStages + 2 * kPfBufs + 1);
+    o += 8 * (2 * kPfMaxStages + 2 * 2 + 2);
     L.misc_off = o;
     o += 16;
     L.total = o;
@@ -505,7 +503,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7;
-    const int nbc = N >> 7;                        // 128-row weight tiles (SiLU: 64 gate + 64 up)
+    const int nbc = N >> 8;                        // 256-row weight tiles
     const PfLayout L = pf_layout(NS, E);
     int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
     int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
@@ -515,8 +513,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
-    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + kPfBufs + a); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 2 * kPfBufs);
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
+    const uint32_t epi_bar = drain_bar + 8u;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
     const uint32_t stage_base = smem_addr(smem + L.stages_off);
@@ -526,11 +525,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
-        for (int a = 0; a < kPfBufs; ++a) {
+        for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), kPfEpi);
         }
         mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kPfEpi);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -571,15 +571,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (elect_one()) {
             tma_prefetch_desc(&tm_w);
             tma_prefetch_desc(&tm_a);
-            const uint64_t pol = policy_evict_last();      // reused across the expert's tiles
+            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
+            const uint64_t pol_a = policy_evict_last();
             int it = 0;
             RingPos rp;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 int e, row0, rows, nb;
                 decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
-                const int w0 = PAIR ? e * N + nb * 64 : e * N + nb * 128;
-                const int w1 = e * N + (N >> 1) + nb * 64;
+                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
+                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
                 for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
                     const int s = rp.slot;
                     if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
@@ -588,13 +589,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     const uint32_t dst = stage_base + s * kPfStage;
                     mbar_expect_tx(full_bar(s), kPfStage);
-                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol);
-                    if (PAIR) {
-                        tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol);
-                        tma_load_2d_hint(dst + 16384 + 8192, &tm_w, kb * 128, w1, full_bar(s), pol);
-                    } else {
-                        tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol);
-                    }
+                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
                 }
             }
             for (int i = max(0, it - NS); i < it; ++i)
@@ -603,11 +600,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     } else if (warp == 1) {
         // ================= MMA issuer =================
         if (elect_one()) {
-            constexpr uint32_t idesc = make_idesc(128, 128, 0, 0);
+            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
             RingPos rs, ra;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(kPfBufs)) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
                     const int s = rs.slot, a = ra.slot;
                     if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
                         !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
@@ -616,7 +613,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t st = stage_base + s * kPfStage;
-                    const uint32_t d = tmem_base + a * 128;
+                    const uint32_t d = tmem_base + a * 256;
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
                         mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
@@ -630,7 +627,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     } else {
         // ================= epilogue: promotion + store =================
-        const int h = (warp - 2) >> 2;           // column half of the 128-column tile
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
         const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
@@ -641,91 +638,75 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
             const bool live = r < rows;
             const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
-            // weight blocks of this thread's columns: plain -> block nb (all 64
-            // columns); SiLU -> gate block nb/2 (32 cols) and up block N/256 + nb/2
-            const int blk0 = PAIR ? (nb >> 1) : nb;
-            const int blk1 = PAIR ? (N >> 8) + (nb >> 1) : nb;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
             const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
             const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
-            // TMEM columns of this thread: plain -> [64h, 64h+64);
-            // SiLU -> gate [32h, 32h+32) and up [64 + 32h, 64 + 32h + 32)
-            const uint32_t c0 = PAIR ? 32 * h : 64 * h;
-            const uint32_t c1 = PAIR ? 64 + 32 * h : 64 * h + 32;
-            float acc[64];
+            float acc0[64], acc1[64];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-            constexpr int kPre = 4;                // scales prefetched kPre K blocks ahead
-            float na[kPre], n0[kPre], n1[kPre];
-#pragma unroll
-            for (int j = 0; j < kPre; ++j) {
-                const bool in = j < nk;
-                na[j] = (in && live) ? __ldg(as_row + j) : 0.0f;
-                n0[j] = in ? __ldg(ws0 + j) : 0.0f;
-                n1[j] = in ? __ldg(ws1 + j) : 0.0f;
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
             }
             bool ok = true;
-            for (int kc = 0; kc < nk && ok; kc += kPre) {
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                       args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
 #pragma unroll
-                for (int j = 0; j < kPre; ++j) {
-                    if (kc + j >= nk) break;
-                    const float s0 = na[j] * n0[j], s1 = na[j] * n1[j];
-                    {
-                        const int kn = kc + kPre + j;
-                        const bool in = kn < nk;
-                        na[j] = (in && live) ? __ldg(as_row + kn) : 0.0f;
-                        n0[j] = in ? __ldg(ws0 + kn) : 0.0f;
-                        n1[j] = in ? __ldg(ws1 + kn) : 0.0f;
-                    }
-                    ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
-                                                           args.ctl, SITE_TFULL));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t tb = tmem_base + lane_addr + ra.slot * 128;
-                    float v[64];
-                    tmem_ld32(tb + c0, v);
-                    tmem_ld32(tb + c1, v + 32);
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
                     tmem_ld_wait();
-                    tc_fence_before();
-                    mbar_arrive(tempty_bar(ra.slot));
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        acc[i] = fmaf(v[i], s0, acc[i]);
-                        acc[32 + i] = fmaf(v[32 + i], s1, acc[32 + i]);
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
                     }
-                    ra.advance(kPfBufs);
                 }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(ra.slot));
             }
             if (!ok) break;
             if (live) {
                 __nv_bfloat16* o = args.out + (size_t)(row0 + r) * ldo;
                 if (PAIR) {
-                    // tile nb holds gate/up columns [64nb, 64nb + 64); this thread 32 of them
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 64 + 32 * h);
-#pragma unroll
-                    for (int c = 0; c < 32; c += 8) {
-                        uint4 pk;
-                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b = __floats2bfloat162_rn(
-                                silu_mul(acc[c + 2 * j], acc[32 + c + 2 * j]),
-                                silu_mul(acc[c + 2 * j + 1], acc[32 + c + 2 * j + 1]));
-                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
-                        }
-                        dst[c >> 3] = pk;
-                    }
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + 64 * h);
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
 #pragma unroll
                     for (int c = 0; c < 64; c += 8) {
                         uint4 pk;
                         uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b = __floats2bfloat162_rn(acc[c + 2 * j], acc[c + 2 * j + 1]);
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
                             pw[j] = *reinterpret_cast<const uint32_t*>(&b);
                         }
                         dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
                     }
                 }
             }
@@ -747,7 +728,7 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
                        int N, int K, int E, cudaStream_t stream) {
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
-                          PAIR ? 64 : 128, true);
+                          128, true);
     if (rc != FERRET_OK) return rc;
     rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
     if (rc != FERRET_OK) return rc;
@@ -791,7 +772,7 @@ int pick_tile(int M, int E, int flags, bool pair) {
 bool use_prefill(int M, int E, int flags, int N) {
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
     if (nt == 0) nt = ((M + E - 1) / std::max(E, 1)) > 48 ? 128 : 0;
-    return nt == 128 && N % 128 == 0;
+    return nt == 128 && N % 256 == 0;
 }
 
 }  // namespace
