@@ -34,6 +34,8 @@ SIGNATURES = {
     "ferret_fp8_grouped_gemm_nt_contiguous": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _sz, _p]),
     "ferret_fp8_grouped_gemm_workspace_size": (_sz, [_i, _i]),
+    "ferret_fp8_grouped_gemm_scatter": (
+        _i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p]),
     "ferret_int4_blob_bytes": (_sz, [_i, _i, _i]),
     "ferret_int4_repack_w13": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "ferret_int4_moe_w13_workspace_size": (_sz, [_i, _i, _i]),

@@ -51,6 +51,8 @@ struct GemmArgs {
     const int32_t* seg;    // offsets[E+1] (seg_pairs == 0) or [E][2] (start, count)
     int seg_pairs;
     __nv_bfloat16* out;
+    const int32_t* out_rows;   // nullable: output row of expert-sorted row i is out_rows[i]
+    int out_total;             // rows of `out` when out_rows is set (others are skipped)
     int M, N, K, E;
     int stages;
     DevCtl ctl;
@@ -340,12 +342,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             // store: this thread owns output column n for the tile's rows
             const int n = nb * 128 + q * 32 + lane;
-            __nv_bfloat16* o = args.out + (size_t)row0 * ldo + n;
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
                 if (j < rows) {
+                    int orow = row0 + j;
+                    if (args.out_rows) {
+                        orow = __ldg(args.out_rows + row0 + j);
+                        if (orow < 0 || orow >= args.out_total) continue;
+                    }
                     const float val = PAIR ? silu_mul(acc_g[j], acc_u[PAIR ? j : 0]) : acc_g[j];
-                    o[(size_t)j * ldo] = __float2bfloat16_rn(val);
+                    args.out[(size_t)orow * ldo + n] = __float2bfloat16_rn(val);
                 }
             }
         }
@@ -412,7 +418,8 @@ __global__ void __launch_bounds__(kSegThreads, 1)
 template <int NT, bool PAIR>
 int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
-               int K, int E, cudaStream_t stream) {
+               int K, int E, cudaStream_t stream, const int32_t* out_rows = nullptr,
+               int out_total = 0) {
     using C = Cfg<NT, PAIR>;
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
@@ -438,6 +445,8 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     g.seg = seg;
     g.seg_pairs = seg_pairs;
     g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_rows = out_rows;
+    g.out_total = out_total;
     g.M = M;
     g.N = N;
     g.K = K;
@@ -673,8 +682,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 mbar_arrive(tempty_bar(ra.slot));
             }
             if (!ok) break;
-            if (live) {
-                __nv_bfloat16* o = args.out + (size_t)(row0 + r) * ldo;
+            int orow = row0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + row0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            if (live && orow >= 0) {
+                __nv_bfloat16* o = args.out + (size_t)orow * ldo;
                 if (PAIR) {
                     uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
 #pragma unroll
@@ -725,7 +739,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 template <bool PAIR>
 int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                        const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
-                       int N, int K, int E, cudaStream_t stream) {
+                       int N, int K, int E, cudaStream_t stream, const int32_t* out_rows = nullptr,
+                       int out_total = 0) {
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
                           128, true);
@@ -747,6 +762,8 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
     g.seg = seg;
     g.seg_pairs = seg_pairs;
     g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_rows = out_rows;
+    g.out_total = out_total;
     g.M = M;
     g.N = N;
     g.K = K;
@@ -925,6 +942,52 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
                         : launch_fp8<64, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
         case 128:
             return launch_fp8<128, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s);
+        default:
+            return FERRET_ERR_SHAPE;
+    }
+}
+
+
+// Scatter-output form: rows of expert segment e are [off[e], off[e+1]) of A as
+// usual, but expert-sorted row i is written to output row out_rows[i] (rows
+// outside [0, out_total) are skipped).  With out_rows = the permutation's
+// sorted_rows this writes the W13 result straight into (token, slot) order.
+extern "C" int ferret_fp8_grouped_gemm_scatter(const void* a_fp8, const float* a_scale,
+                                               const void* w_fp8, const float* w_scale,
+                                               void* out_bf16, const int32_t* expert_offsets,
+                                               const int32_t* out_rows, int M, int out_total, int N,
+                                               int K, int E, int flags, void* stream) {
+    const bool pair = (flags & FERRET_SILU_MUL) != 0;
+    if (M < 0 || out_total < 0 || N <= 0 || K <= 0 || E <= 0 || E > kMaxE) return FERRET_ERR_SHAPE;
+    if (K % 128 || N % 128 || (pair && N % 256) || K / 128 > kMaxNK) return FERRET_ERR_SHAPE;
+    if ((long long)E * N >= (1ll << 31) || (long long)M * K >= (1ll << 40)) return FERRET_ERR_SHAPE;
+    if (M == 0 || out_total == 0) return FERRET_OK;
+    if (!a_fp8 || !a_scale || !w_fp8 || !w_scale || !out_bf16 || !expert_offsets || !out_rows)
+        return FERRET_ERR_NULL;
+    if (!aligned16(a_fp8) || !aligned16(w_fp8) || !aligned16(out_bf16) ||
+        (reinterpret_cast<uintptr_t>(a_scale) & 3u) || (reinterpret_cast<uintptr_t>(w_scale) & 3u))
+        return FERRET_ERR_ALIGN;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    cudaStream_t s = as_stream(stream);
+    if (use_prefill(M, E, flags, N))
+        return pair ? launch_fp8_prefill<true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16,
+                                               expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
+                    : launch_fp8_prefill<false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16,
+                                                expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
+    switch (pick_tile(M, E, flags, pair)) {
+        case 16:
+            return pair ? launch_fp8<16, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
+                        : launch_fp8<16, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
+        case 32:
+            return pair ? launch_fp8<32, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
+                        : launch_fp8<32, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
+        case 64:
+            return pair ? launch_fp8<64, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
+                        : launch_fp8<64, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
+        case 128:
+            return launch_fp8<128, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
         default:
             return FERRET_ERR_SHAPE;
     }

@@ -5,8 +5,9 @@ gloo on CPU for the host-logic tests).
 
 One rank per GPU.  Rank r owns E/G experts (contiguous ids by default, or a
 placement table, e.g. the balanced one from ``balanced_placement``) and only
-holds their weights.  A forward step on every rank:
+holds their weights.  Two exchange schemes, chosen by batch size:
 
+* "a2a" (prefill-sized batches), every step:
   1. remap expert ids to placement order and permute the local (token, slot)
      pairs by expert -- expert-sorted order is also destination-rank order;
   2. all_to_all of the per-expert counts (E ints), one device->host copy of
@@ -15,6 +16,13 @@ holds their weights.  A forward step on every rank:
   4. locally: permute the received rows by local expert, gathered FP8
      quantization, grouped GEMM (the CUDA kernels);
   5. un-permute, combine all_to_all back, scatter into (token, slot) order.
+* "gather" (decode-sized batches, no host synchronisation, fixed sizes):
+  1. all_gather of every rank's token rows and top-k ids;
+  2. locally: keep the pairs routed to this rank's experts, permute, gathered
+     FP8 quantization, and the scatter-output grouped GEMM writing each row
+     straight into a zeroed (token, slot)-ordered buffer of the whole batch;
+  3. reduce_scatter (sum) of that buffer returns each rank its own rows --
+     every pair has exactly one non-zero contributor, so the sum is exact.
 
 The reference has no multi-GPU implementation of this path; parity is the
 single-GPU result for every (token, slot) pair.
@@ -40,6 +48,10 @@ class CudaKernels:
 
     def quant(self, x: torch.Tensor, rows: torch.Tensor, div: int):
         return self.ops.per_token_cast_to_fp8(x, rows, div)
+
+    def gemm_scatter(self, q, s, W, Ws, offsets, out_rows, out, silu: bool):
+        if q.shape[0]:
+            self.ops.m_grouped_fp8_gemm_scatter((q, s), (W, Ws), out, offsets, out_rows, silu=silu)
 
     def gemm(self, q, s, W, Ws, offsets, silu: bool):
         E, N, _ = W.shape
@@ -86,8 +98,13 @@ class ExpertParallelW13:
     owner-order table (global expert id of every slot; default identity).
     """
 
+    GATHER_BYTES = 64 << 20    # dense combine buffer above which "auto" uses a2a
+
     def __init__(self, W_local, Ws_local, E: int, group=None, silu: bool = False,
-                 placement: torch.Tensor | None = None, kernels=None):
+                 placement: torch.Tensor | None = None, kernels=None, mode: str = "auto"):
+        if mode not in ("auto", "a2a", "gather"):
+            raise ValueError(mode)
+        self.mode = mode
         self.group = group
         self.G = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -122,16 +139,61 @@ class ExpertParallelW13:
                 timers: StepTimers | None = None) -> torch.Tensor:
         """hidden bf16 [T, K], topk_ids int32 [T, topk] (global expert ids) ->
         bf16 [T*topk, N or N/2] in (token, slot) order; pairs with an invalid
-        expert id get zero rows."""
+        expert id get zero rows.  Every rank passes the same T."""
+        T, topk = topk_ids.shape
+        N = self.W.shape[1]
+        n_out = N // 2 if self.silu else N
+        mode = self.mode
+        if mode == "auto":
+            mode = "gather" if self.G * T * topk * n_out * 2 <= self.GATHER_BYTES else "a2a"
+        if mode == "gather":
+            return self._forward_gather(hidden, topk_ids, timers)
+        return self._forward_a2a(hidden, topk_ids, timers)
+
+    def _remap(self, ids: torch.Tensor) -> torch.Tensor:
+        if self.remap is None:
+            return ids
+        valid = (ids >= 0) & (ids < self.E)
+        return torch.where(valid, self.remap[ids.clamp(0, self.E - 1).long()], -1).to(torch.int32)
+
+    def _forward_gather(self, hidden, topk_ids, timers):
         T, topk = topk_ids.shape
         K = hidden.shape[1]
         N = self.W.shape[1]
         n_out = N // 2 if self.silu else N
         dev = hidden.device
-        ids = topk_ids
-        if self.remap is not None:
-            valid = (ids >= 0) & (ids < self.E)
-            ids = torch.where(valid, self.remap[ids.clamp(0, self.E - 1).long()], -1).to(torch.int32)
+        ids = self._remap(topk_ids).contiguous()
+        if self.G > 1:
+            all_h = torch.empty(self.G * T, K, dtype=hidden.dtype, device=dev)
+            dist.all_gather_into_tensor(all_h.view(torch.uint8), hidden.contiguous().view(torch.uint8),
+                                        group=self.group)
+            all_ids = torch.empty(self.G * T, topk, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(all_ids, ids, group=self.group)
+        else:
+            all_h, all_ids = hidden, ids
+        loc = all_ids - self.rank * self.El
+        local = torch.where((all_ids >= 0) & (loc >= 0) & (loc < self.El), loc, -1).to(torch.int32)
+        rows, offs = self.kernels.permute(local.contiguous(), self.El)
+        q, s = self.kernels.quant(all_h, rows, topk)
+        dense = torch.zeros(self.G * T * topk, n_out, dtype=torch.bfloat16, device=dev)
+        if timers is not None and timers.gemm_start is not None:
+            timers.gemm_start.record()
+        self.kernels.gemm_scatter(q, s, self.W, self.Ws, offs, rows, dense, self.silu)
+        if timers is not None and timers.gemm_end is not None:
+            timers.gemm_end.record()
+        if self.G == 1:
+            return dense
+        out = torch.empty(T * topk, n_out, dtype=torch.bfloat16, device=dev)
+        dist.reduce_scatter_tensor(out, dense, group=self.group)
+        return out
+
+    def _forward_a2a(self, hidden, topk_ids, timers):
+        T, topk = topk_ids.shape
+        K = hidden.shape[1]
+        N = self.W.shape[1]
+        n_out = N // 2 if self.silu else N
+        dev = hidden.device
+        ids = self._remap(topk_ids)
         rows, offs = self.kernels.permute(ids.contiguous(), self.E)
         counts = (offs[1:] - offs[:-1]).contiguous()
         recv_counts = torch.empty_like(counts)

@@ -130,6 +130,34 @@ def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.T
         "ferret_fp8_grouped_gemm_nt_contiguous")
 
 
+def m_grouped_fp8_gemm_scatter(a, b, out: torch.Tensor, expert_offsets: torch.Tensor,
+                               out_rows: torch.Tensor, silu: bool = False, tile: int = 0) -> None:
+    """Grouped FP8 GEMM whose expert-sorted row i lands in out[out_rows[i]]
+    (rows of out_rows outside [0, out.shape[0]) are skipped)."""
+    A, A_scale = a
+    W, W_scale = b
+    if A.dtype == torch.float8_e4m3fn:
+        A = A.view(torch.uint8)
+    if W.dtype == torch.float8_e4m3fn:
+        W = W.view(torch.uint8)
+    _need(A, torch.uint8, "A", 2)
+    _need(W, torch.uint8, "W", 3)
+    _need(A_scale, torch.float32, "A_scale", 2)
+    _need(W_scale, torch.float32, "W_scale", 3)
+    _need(out, torch.bfloat16, "out", 2)
+    _need(expert_offsets, torch.int32, "expert_offsets", 1)
+    _need(out_rows, torch.int32, "out_rows", 1)
+    M, K = A.shape
+    E, N, _ = W.shape
+    if out.shape[1] != (N // 2 if silu else N):
+        raise ValueError("out has the wrong number of columns")
+    flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+    check(lib().ferret_fp8_grouped_gemm_scatter(
+        _ptr(A), _ptr(A_scale), _ptr(W), _ptr(W_scale), _ptr(out), _ptr(expert_offsets),
+        _ptr(out_rows), M, out.shape[0], N, K, E, flags, _stream()),
+        "ferret_fp8_grouped_gemm_scatter")
+
+
 class W13Buffers:
     """Preallocated intermediates of the fused W13 path for fixed sizes."""
 

@@ -132,6 +132,23 @@ FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous(const void* a_fp8, const fl
                                           int M, int N, int K, int E, int flags, void* workspace,
                                           size_t ws_bytes, void* stream);
 
+/*
+ * Scatter-output form of the FP8 grouped GEMM: expert segments from
+ * expert_offsets [E+1] over the rows of a_fp8 [M, K], and expert-sorted row i
+ * written to output row out_rows[i] of out_bf16 [out_total, N or N/2] (rows
+ * whose out_rows entry lies outside [0, out_total) are skipped).  With
+ * out_rows = ferret_moe_permute's sorted_rows the result lands directly in
+ * (token, slot) order -- the order Marlin's MoE output uses
+ * (baselines/kimi-moe-w13-int4/baseline_marlin.py:140-168) and the one the
+ * expert-parallel combine needs.  Same limits as
+ * ferret_fp8_grouped_gemm_nt_contiguous.
+ */
+FERRET_API int ferret_fp8_grouped_gemm_scatter(const void* a_fp8, const float* a_scale,
+                                               const void* w_fp8, const float* w_scale,
+                                               void* out_bf16, const int32_t* expert_offsets,
+                                               const int32_t* out_rows, int M, int out_total, int N,
+                                               int K, int E, int flags, void* stream);
+
 /* Workspace bytes ferret_fp8_grouped_gemm_nt_contiguous needs when
  * expert_offsets is NULL. */
 FERRET_API size_t ferret_fp8_grouped_gemm_workspace_size(int M, int E);

@@ -29,6 +29,12 @@ class OracleKernels:
         q, s = O.quant_act_fp8_1x128(x.view(torch.int16).numpy().view(np.uint16), rows.numpy(), div)
         return torch.from_numpy(q), torch.from_numpy(s)
 
+    def gemm_scatter(self, q, s, W, Ws, offsets, out_rows, out, silu):
+        dense = self.gemm(q, s, W, Ws, offsets, silu)
+        R = int(offsets[-1])
+        rows = out_rows[:R].long()
+        out[rows] = dense[:R]
+
     def gemm(self, q, s, W, Ws, offsets, silu):
         offs = offsets.numpy()
         mi = np.repeat(np.arange(len(offs) - 1), np.diff(offs)).astype(np.int32)
@@ -65,7 +71,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, silu, balanced, q):
+def _worker(rank, world, port, silu, balanced, q, mode="auto"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -81,7 +87,7 @@ def _worker(rank, world, port, silu, balanced, q):
         mine = table[rank * El:(rank + 1) * El].long()
         t0, t1 = rank * T // world, (rank + 1) * T // world
         ep = ExpertParallelW13(W[mine], Ws[mine], E, silu=silu, placement=placement,
-                               kernels=OracleKernels())
+                               kernels=OracleKernels(), mode=mode)
         out = ep.forward(hidden[t0:t1], ids[t0:t1])
         outs = [torch.empty((T // world) * TOPK, out.shape[1] * 2, dtype=torch.uint8)
                 for _ in range(world)]
@@ -95,12 +101,15 @@ def _worker(rank, world, port, silu, balanced, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,silu,balanced", [(2, False, False), (2, True, True), (4, False, True)])
-def test_ep_matches_single_process(world, silu, balanced):
+@pytest.mark.parametrize("world,silu,balanced,mode", [
+    (2, False, False, "a2a"), (2, True, True, "a2a"), (4, False, True, "a2a"),
+    (2, False, False, "gather"), (4, True, True, "gather"),
+])
+def test_ep_matches_single_process(world, silu, balanced, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, silu, balanced, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, silu, balanced, q, mode))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -39,11 +39,14 @@ def _worker(rank, world, port, q):
         out, rows, _ = ops.fp8_moe_w13(hidden, ids, W, Ws)
         ref = torch.empty_like(out)
         ref[rows.long()] = out
-        for placement in (None, balanced_placement(torch.bincount(ids.reshape(-1).cpu(), minlength=E), world)):
+        cases = [(p, m) for p in (None, balanced_placement(torch.bincount(ids.reshape(-1).cpu(), minlength=E), world))
+                 for m in ("a2a", "gather")]
+        for placement, mode in cases:
             table = placement if placement is not None else torch.arange(E)
             El, Tl = E // world, T // world
             mine = table[rank * El:(rank + 1) * El].long().to(dev)
-            ep = ExpertParallelW13(W[mine].contiguous(), Ws[mine].contiguous(), E, placement=placement)
+            ep = ExpertParallelW13(W[mine].contiguous(), Ws[mine].contiguous(), E, placement=placement,
+                                   mode=mode)
             got = ep.forward(hidden[rank * Tl:(rank + 1) * Tl].contiguous(),
                              ids[rank * Tl:(rank + 1) * Tl].contiguous())
             torch.cuda.synchronize()
@@ -69,7 +72,7 @@ def test_ep_two_gpus_matches_single_gpu(cuda_device):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in range(2)]
+    results = [q.get(timeout=300) for _ in range(4)]
     for p in procs:
         p.join(timeout=120)
     assert all(r is True for r in results), results

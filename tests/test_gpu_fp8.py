@@ -312,3 +312,26 @@ def test_w13_path_dsv3_prefill_full_size(ops):
             err = O.rel_err(got[r0:r1], ref)
             assert err["nan"] == 0 and err["max_rel"] < TOL, (silu, int(e), err)
     assert ops.last_device_status() == 0
+
+
+@pytest.mark.parametrize("silu,tile", [(False, 0), (True, 16), (False, 128), (True, 128)])
+def test_scatter_gemm_token_order(ops, silu, tile):
+    """The scatter-output GEMM writes row i of the expert-sorted operand to
+    out[sorted_rows[i]]: the (token, slot) order, bit-identical to the
+    contiguous GEMM's rows moved there."""
+    from ferret_b200 import data
+    cfg = data.CONFIGS["cpu_fp8"]
+    dev = torch.device("cuda")
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K).to(dev)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, "zipf").to(dev)
+    ids[3, 1] = -1
+    out, rows, offs = ops.fp8_moe_w13(hidden, ids, W, Ws, silu=silu, tile=tile)
+    q, s = ops.per_token_cast_to_fp8(hidden, rows, cfg.topk)
+    tok = torch.full((cfg.R, out.shape[1]), 7.0, dtype=torch.bfloat16, device=dev)
+    ops.m_grouped_fp8_gemm_scatter((q, s), (W, Ws), tok, offs, rows, silu=silu, tile=tile)
+    torch.cuda.synchronize()
+    R = int(offs[-1])
+    want = torch.full_like(tok, 7.0)
+    want[rows[:R].long()] = out[:R]
+    assert torch.equal(tok.view(torch.int16), want.view(torch.int16))
