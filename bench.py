@@ -208,6 +208,32 @@ def cpu_baseline(a_q, a_scale, W, W_s, offsets, cfg, budget_s=12.0, max_experts=
 # our arm, one GPU
 # ---------------------------------------------------------------------------
 
+def int4_cpu_baseline(hidden, ids, samples, cfg, budget_s=12.0):
+    """The torch CPU fp32 INT4 path (dequantize-then-matmul) on a bounded
+    sample: the experts in `samples` ({expert: (raw, scales)} host copies) with
+    all their routed rows, until ~budget_s of CPU work."""
+    import torch
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    flat = ids.reshape(-1).cpu()
+    h = hidden.cpu()
+    flops, t_sum, rows_done, n = 0.0, 0.0, 0, 0
+    for e, (raw_e, sc_e) in samples.items():
+        rows = torch.nonzero(flat == e).flatten() // cfg.topk
+        t1 = time.perf_counter()
+        O.int4_w13_torch_cpu(h[rows], raw_e, sc_e, silu=cfg.silu)
+        t_sum += time.perf_counter() - t1
+        flops += 2.0 * len(rows) * cfg.N * cfg.K
+        rows_done += len(rows)
+        n += 1
+        if t_sum > budget_s:
+            break
+    return {"value": flops / t_sum / 1e12, "unit": "TFLOPS", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} active experts ({rows_done} routed rows), torch fp32 INT4 "
+                      f"dequantize-then-matmul per expert, {t_sum:.1f} s"}
+
+
 def run_single(args, cfg):
     import torch
     from ferret_b200 import build, data, ops
@@ -311,7 +337,7 @@ def run_single(args, cfg):
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "hbm_gbs_step": round(byts / (ms * 1e-3) / 1e9, 1),
-        "roofline": dict(rl, traffic=read_traffic(f"{rl['kernel']}_{cfg.name}")),
+        "roofline": dict(rl, traffic=read_traffic(f"{rl['kernel'].removesuffix('_kernel')}_{cfg.name}")),
         "e2e": {"value": round(flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                 "ms_per_step": round(e_ms, 4),
                 "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
@@ -333,9 +359,14 @@ def run_single_int4(args, cfg):
     torch.cuda.set_device(dev)
     raw, scales = data.int4_weights(cfg.E, cfg.N, cfg.K, device=dev)
     packed = ops.Int4W13Weights(raw, scales)
-    del raw, scales
     hidden = data.activations(cfg.T, cfg.K).to(dev)
     ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
+    samples = {}
+    if not args.no_cpu_baseline and not args.gemm_only:
+        # host copies of the first active experts for the CPU baseline
+        act = torch.nonzero(torch.bincount(ids.reshape(-1).long(), minlength=cfg.E)).flatten()
+        samples = {int(e): (raw[e].cpu(), scales[e].cpu()) for e in act[:32]}
+    del raw, scales
     n_out = cfg.N // 2 if cfg.silu else cfg.N
     out = torch.zeros(cfg.R, n_out, dtype=torch.bfloat16, device=dev)
     ws = torch.empty(ops.lib().ferret_int4_moe_w13_workspace_size(cfg.T, cfg.topk, cfg.K),
@@ -393,7 +424,7 @@ def run_single_int4(args, cfg):
     e_ms = sum(e2e_ms) / len(e2e_ms)
     pk = peaks()
     achieved = byts / (g_ms * 1e-3) / 1e9
-    return {
+    res = {
         "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
         "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -416,9 +447,12 @@ def run_single_int4(args, cfg):
                 "ms_per_step": round(e_ms, 4),
                 "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
                 "d2h_bytes_per_step": h_out.numel() * 2},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 3 * args.steps,   # permute, row gather, INT4 GEMM
         "clocks": clk,
     }
+    if samples:
+        res["cpu_baseline"] = int4_cpu_baseline(hidden, ids, samples, cfg)
+    return res
 
 
 # ---------------------------------------------------------------------------

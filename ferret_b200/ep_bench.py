@@ -5,6 +5,9 @@ Launched by torchrun (one process per GPU, NCCL).  Rank r owns E/G experts
 T/G of the tokens; one step = ExpertParallelW13.forward (permute, count
 exchange, bf16 dispatch all_to_all, local permute + FP8 quant + grouped GEMM,
 combine all_to_all).  Strong scaling: the global batch is fixed as G grows.
+Decode-sized batches (the sync-free "gather" exchange) run each step as one
+CUDA graph replay, the NCCL collectives inside the graph; prefill-sized ones
+("a2a", one host sync per step for the splits) run eagerly.
 Timing: CUDA events per step on each rank's stream, 256 MB L2 flush between
 steps, barrier + synchronize around the timed region, max over ranks.
 """
@@ -62,13 +65,32 @@ def run(args, cfg):
         ids = ids_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
         hidden = hidden_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
         ep = ExpertParallelW13(W, Ws, cfg.E, silu=cfg.silu, placement=placement)
+        n_out = cfg.N // 2 if cfg.silu else cfg.N
+        graphed = ep.G * Tl * cfg.topk * n_out * 2 <= ep.GATHER_BYTES   # sync-free gather mode
 
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        stream = torch.cuda.current_stream()
         for _ in range(args.warmup):
             ep.forward(hidden, ids)
         torch.cuda.synchronize()
         dist.barrier()
+        graph = None
+        if graphed:
+            # the whole step -- collectives included -- as one CUDA graph; every
+            # rank captures the same sequence of collectives
+            # external events become record nodes of the graph, so the local
+            # GEMM stays timed on replay
+            tm_g = StepTimers(torch.cuda.Event(enable_timing=True, external=True),
+                              torch.cuda.Event(enable_timing=True, external=True))
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    out_static = ep.forward(hidden, ids, timers=tm_g)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            dist.barrier()
+        stream = torch.cuda.current_stream()
 
         K = args.steps
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -80,16 +102,26 @@ def run(args, cfg):
         dist.barrier()
         if clocks:
             clocks.start()
+        gemm_list = []
         for i in range(K):
             flush.zero_()
             ev[i][0].record(stream)
-            out = ep.forward(hidden, ids, timers=tm[i])
+            if graph is not None:
+                graph.replay()
+                out = out_static
+            else:
+                out = ep.forward(hidden, ids, timers=tm[i])
             ev[i][1].record(stream)
+            if graph is not None:
+                torch.cuda.synchronize()
+                gemm_list.append(tm_g.gemm_start.elapsed_time(tm_g.gemm_end))
         torch.cuda.synchronize()
         dist.barrier()
         clk = clocks.stop() if clocks else None
         step_ms = sum(a.elapsed_time(b) for a, b in ev) / K
-        gemm_ms = sum(t.gemm_start.elapsed_time(t.gemm_end) for t in tm) / K
+        if graph is None:
+            gemm_list = [t.gemm_start.elapsed_time(t.gemm_end) for t in tm]
+        gemm_ms = sum(gemm_list) / K
 
         # e2e: host buffers in, host buffer out, through the same public API
         h_hidden = hidden.cpu().pin_memory()
@@ -102,9 +134,15 @@ def run(args, cfg):
         for i in range(K):
             flush.zero_()
             ev2[i][0].record(stream)
-            d_hidden.copy_(h_hidden, non_blocking=True)
-            d_ids.copy_(h_ids, non_blocking=True)
-            o = ep.forward(d_hidden, d_ids)
+            if graph is not None:
+                hidden.copy_(h_hidden, non_blocking=True)     # the graph's static inputs
+                ids.copy_(h_ids, non_blocking=True)
+                graph.replay()
+                o = out_static
+            else:
+                d_hidden.copy_(h_hidden, non_blocking=True)
+                d_ids.copy_(h_ids, non_blocking=True)
+                o = ep.forward(d_hidden, d_ids)
             h_out.copy_(o, non_blocking=True)
             ev2[i][1].record(stream)
         torch.cuda.synchronize()
@@ -158,7 +196,10 @@ def run(args, cfg):
                     "h2d_bytes_per_step": (h_hidden.numel() * 2 + h_ids.numel() * 4) * G,
                     "d2h_bytes_per_step": h_out.numel() * 2 * G},
             "gpu_launches": 4 * K,
+            "cuda_graph": graph is not None,
             "clocks": clk,
         }
     finally:
+        graph = None        # a graph holding NCCL work must be released before teardown
+        torch.cuda.synchronize()
         dist.destroy_process_group()

@@ -303,3 +303,24 @@ def fp8_w13_torch_cpu(a_q, a_scale, w_q, w_scale, offsets, experts, silu=False):
             acc = g / (1.0 + torch.exp(-g)) * u
         out[e] = acc
     return out
+
+
+def int4_w13_torch_cpu(x_bf16, raw_e, scales_e, silu=True):
+    """One expert of the INT4 W4A16 W13 on the host cores with torch, fp32
+    dequantize-then-matmul as in correctness/compare_marlin_vs_ref.py:44-100:
+    w[k, n] = bf16((nibble(k, n) - 8) * scale[k // 32, n]), out = x @ w.
+
+    x_bf16 [rows, K] bf16; raw_e int32 [K/8, N] (nibble s of word k8 is
+    k = 8*k8 + s); scales_e bf16 [K/32, N].  Returns fp32 [rows, N or N/2].
+    """
+    import torch
+    K8, N = raw_e.shape
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32).view(1, 8, 1)
+    nib = (raw_e.view(K8, 1, N) >> shifts) & 0xF                          # [K/8, 8, N]
+    w = (nib.reshape(K8 * 8, N).float() - 8.0) * scales_e.float().repeat_interleave(32, 0)
+    w = w.to(torch.bfloat16).float()
+    acc = x_bf16.float() @ w
+    if silu:
+        g, u = acc[:, : N // 2], acc[:, N // 2:]
+        acc = g / (1.0 + torch.exp(-g)) * u
+    return acc
