@@ -45,6 +45,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--placement", choices=["contiguous", "balanced"], default="contiguous",
                     help="expert placement for N>1 (balanced = greedy LPT on the routing histogram)")
+    ap.add_argument("--ep-mode", choices=["p2p", "gather", "a2a", "auto"], default="p2p",
+                    help="N>1 exchange: p2p = peer-memory kernels (library ferret_ep_*); "
+                         "gather / a2a / auto = torch.distributed NCCL collectives")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="profiling aid: run N bare GEMM launches and exit")
     return ap.parse_args()
@@ -342,7 +345,9 @@ def run_single(args, cfg):
                 "ms_per_step": round(e_ms, 4),
                 "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
                 "d2h_bytes_per_step": h_out.numel() * 2},
-        "gpu_launches": 3 * args.steps,
+        # permute (1, or count/scan/scatter), quant (1, or quant-once + gather), GEMM
+        "gpu_launches": ((3 if bufs.perm_ws_bytes else 1) + (2 if bufs.quant_once else 1) + 1)
+                        * args.steps,
         "clocks": clk,
         "output_finite": out_ok,
     }

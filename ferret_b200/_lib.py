@@ -30,7 +30,9 @@ SIGNATURES = {
     "ferret_last_device_status": (_i, [_p, ctypes.POINTER(ctypes.c_int32)]),
     "ferret_selftest_wait_timeout": (_i, [ctypes.c_ulonglong, _p]),
     "ferret_moe_permute": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
+    "ferret_moe_permute_workspace_size": (_sz, [_i, _i, _i]),
     "ferret_quant_act_fp8_1x128": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+    "ferret_fp8_gather_rows": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _sz, _p]),
     "ferret_fp8_grouped_gemm_workspace_size": (_sz, [_i, _i]),
@@ -42,6 +44,12 @@ SIGNATURES = {
     "ferret_int4_moe_w13": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous_noalloc": (
         _i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "ferret_ep_handle_bytes": (_sz, []),
+    "ferret_ep_init": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _p, _p, ctypes.POINTER(_p)]),
+    "ferret_ep_connect": (_i, [_p, _p]),
+    "ferret_ep_w13_forward": (_i, [_p, _p, _p, _i, _p, _p, _p, _p]),
+    "ferret_ep_output_buffer": (_p, [_p]),
+    "ferret_ep_destroy": (_i, [_p]),
 }
 
 

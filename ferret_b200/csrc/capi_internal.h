@@ -39,6 +39,23 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                  const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
                  bool swizzle128);
 
+// Where the grouped GEMM writes expert-sorted row i: row i of `out` (rows ==
+// nullptr), or row rows[i] (skipped outside [0, total)).  With a peer table,
+// output row o goes to row o % peer_rows of buffer peers[o / peer_rows] -- a
+// device array of G pointers, other GPUs' memory included.
+struct OutMap {
+    const int32_t* rows = nullptr;
+    int total = 0;
+    __nv_bfloat16* const* peers = nullptr;
+    int peer_rows = 0;
+};
+
+// FP8 grouped GEMM launch shared by the entry points: picks the prefill kernel
+// or the swap-AB token tile from rows_hint (expected rows holding data) and E.
+int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                 const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
+                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

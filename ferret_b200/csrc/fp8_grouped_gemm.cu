@@ -53,6 +53,8 @@ struct GemmArgs {
     __nv_bfloat16* out;
     const int32_t* out_rows;   // nullable: output row of expert-sorted row i is out_rows[i]
     int out_total;             // rows of `out` when out_rows is set (others are skipped)
+    __nv_bfloat16* const* out_peers;   // nullable: row o lives on buffer o / peer_rows
+    int peer_rows;
     int M, N, K, E;
     int stages;
     DevCtl ctl;
@@ -102,6 +104,17 @@ __host__ __device__ inline Layout make_layout(int stage_bytes, int stages, int N
     o += 16;
     L.total = o;
     return L;
+}
+
+// Address of output row `orow` (row stride ldo): the local matrix, or, with a
+// peer table, row orow % peer_rows of buffer orow / peer_rows (another GPU's
+// memory over NVLink when the table holds peer pointers).
+__device__ __forceinline__ __nv_bfloat16* out_row_ptr(const GemmArgs& a, int orow, int ldo) {
+    if (a.out_peers) {
+        const int g = orow / a.peer_rows;
+        return a.out_peers[g] + (size_t)(orow - g * a.peer_rows) * ldo;
+    }
+    return a.out + (size_t)orow * ldo;
 }
 
 // Tile t -> (expert, first row, rows, n-block).  Tiles are ordered token-tile
@@ -351,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (orow < 0 || orow >= args.out_total) continue;
                     }
                     const float val = PAIR ? silu_mul(acc_g[j], acc_u[PAIR ? j : 0]) : acc_g[j];
-                    args.out[(size_t)orow * ldo + n] = __float2bfloat16_rn(val);
+                    out_row_ptr(args, orow, ldo)[n] = __float2bfloat16_rn(val);
                 }
             }
         }
@@ -418,8 +431,7 @@ __global__ void __launch_bounds__(kSegThreads, 1)
 template <int NT, bool PAIR>
 int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
-               int K, int E, cudaStream_t stream, const int32_t* out_rows = nullptr,
-               int out_total = 0) {
+               int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
     using C = Cfg<NT, PAIR>;
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
@@ -445,8 +457,10 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     g.seg = seg;
     g.seg_pairs = seg_pairs;
     g.out = static_cast<__nv_bfloat16*>(out);
-    g.out_rows = out_rows;
-    g.out_total = out_total;
+    g.out_rows = om.rows;
+    g.out_total = om.total;
+    g.out_peers = om.peers;
+    g.peer_rows = om.peer_rows;
     g.M = M;
     g.N = N;
     g.K = K;
@@ -688,7 +702,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
             if (live && orow >= 0) {
-                __nv_bfloat16* o = args.out + (size_t)orow * ldo;
+                __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
                 if (PAIR) {
                     uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
 #pragma unroll
@@ -739,8 +753,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 template <bool PAIR>
 int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                        const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
-                       int N, int K, int E, cudaStream_t stream, const int32_t* out_rows = nullptr,
-                       int out_total = 0) {
+                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
                           128, true);
@@ -762,8 +775,10 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
     g.seg = seg;
     g.seg_pairs = seg_pairs;
     g.out = static_cast<__nv_bfloat16*>(out);
-    g.out_rows = out_rows;
-    g.out_total = out_total;
+    g.out_rows = om.rows;
+    g.out_total = om.total;
+    g.out_peers = om.peers;
+    g.peer_rows = om.peer_rows;
     g.M = M;
     g.N = N;
     g.K = K;
@@ -793,6 +808,35 @@ bool use_prefill(int M, int E, int flags, int N) {
 }
 
 }  // namespace
+
+int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                 const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
+                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om) {
+    const bool pair = (flags & FERRET_SILU_MUL) != 0;
+    if (use_prefill(rows_hint, E, flags, N))
+        return pair ? launch_fp8_prefill<true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
+                                               N, K, E, s, om)
+                    : launch_fp8_prefill<false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
+                                                N, K, E, s, om);
+#define FERRET_FP8_CASE(NT_)                                                                    \
+    case NT_:                                                                                   \
+        return pair ? launch_fp8<NT_, true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M, \
+                                            N, K, E, s, om)                                     \
+                    : launch_fp8<NT_, false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,\
+                                             N, K, E, s, om);
+    switch (pick_tile(rows_hint, E, flags, pair)) {
+        FERRET_FP8_CASE(16)
+        FERRET_FP8_CASE(32)
+        FERRET_FP8_CASE(64)
+        case 128:
+            return launch_fp8<128, false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M, N,
+                                          K, E, s, om);
+        default:
+            return FERRET_ERR_SHAPE;
+    }
+#undef FERRET_FP8_CASE
+}
+
 }  // namespace ferret
 
 using namespace ferret;
@@ -836,30 +880,10 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
         seg_pairs = 1;
     }
 
-    // many tokens per expert: the prefill kernel (tokens on MMA M, 256 weight rows on N)
-    if (use_prefill(M, E, flags, N))
-        return pair ? launch_fp8_prefill<true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg,
-                                               seg_pairs, M, N, K, E, s)
-                    : launch_fp8_prefill<false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg,
-                                                seg_pairs, M, N, K, E, s);
-    const int nt = pick_tile(M, E, flags, pair);
-#define FERRET_FP8_CASE(NT_)                                                                     \
-    case NT_:                                                                                    \
-        return pair ? launch_fp8<NT_, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, \
-                                            seg_pairs, M, N, K, E, s)                            \
-                    : launch_fp8<NT_, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, \
-                                             seg_pairs, M, N, K, E, s);
-    switch (nt) {
-        FERRET_FP8_CASE(16)
-        FERRET_FP8_CASE(32)
-        FERRET_FP8_CASE(64)
-        case 128:
-            return launch_fp8<128, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg,
-                                          seg_pairs, M, N, K, E, s);
-        default:
-            return FERRET_ERR_SHAPE;
-    }
-#undef FERRET_FP8_CASE
+    // many tokens per expert: the prefill kernel (tokens on MMA M, 256 weight rows on N);
+    // otherwise the swap-AB kernel with a token tile sized to the rows per expert
+    return run_fp8_gemm(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, seg_pairs, M, N, K, E,
+                        flags, M, s, OutMap{});
 }
 
 #include <mutex>
@@ -971,24 +995,9 @@ extern "C" int ferret_fp8_grouped_gemm_scatter(const void* a_fp8, const float* a
     int rc = current_device(&info);
     if (rc != FERRET_OK) return rc;
     cudaStream_t s = as_stream(stream);
-    if (use_prefill(M, E, flags, N))
-        return pair ? launch_fp8_prefill<true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16,
-                                               expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
-                    : launch_fp8_prefill<false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16,
-                                                expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
-    switch (pick_tile(M, E, flags, pair)) {
-        case 16:
-            return pair ? launch_fp8<16, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
-                        : launch_fp8<16, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
-        case 32:
-            return pair ? launch_fp8<32, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
-                        : launch_fp8<32, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
-        case 64:
-            return pair ? launch_fp8<64, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total)
-                        : launch_fp8<64, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
-        case 128:
-            return launch_fp8<128, false>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K, E, s, out_rows, out_total);
-        default:
-            return FERRET_ERR_SHAPE;
-    }
+    OutMap om;
+    om.rows = out_rows;
+    om.total = out_total;
+    return run_fp8_gemm(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, expert_offsets, 0, M, N, K,
+                        E, flags, M, s, om);
 }

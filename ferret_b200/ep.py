@@ -5,7 +5,18 @@ gloo on CPU for the host-logic tests).
 
 One rank per GPU.  Rank r owns E/G experts (contiguous ids by default, or a
 placement table, e.g. the balanced one from ``balanced_placement``) and only
-holds their weights.  Two exchange schemes, chosen by batch size:
+holds their weights.  Three exchange schemes:
+
+* "p2p" (the product path on GPUs; ``PeerContext`` over the library's
+  ferret_ep_* entry points): no collective library on the data path.  Each
+  rank quantizes its own tokens to FP8 once; the owner of an expert pulls the
+  routed FP8 rows from the source rank's memory over NVLink, and the grouped
+  GEMM's epilogue stores each output row straight into the source rank's
+  output buffer.  Bounded device-side flag barriers replace the collectives;
+  no host synchronisation, so a step can be captured in a CUDA graph.
+
+and two over torch.distributed collectives (NCCL on GPUs, gloo on CPU for the
+host-logic tests), chosen by batch size under "auto" when "p2p" is not used:
 
 * "a2a" (prefill-sized batches), every step:
   1. remap expert ids to placement order and permute the local (token, slot)
@@ -29,6 +40,7 @@ single-GPU result for every (token, slot) pair.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -83,6 +95,64 @@ def balanced_placement(counts: torch.Tensor, G: int) -> torch.Tensor:
     return torch.tensor([e for s in slots for e in sorted(s)], dtype=torch.int32)
 
 
+class PeerContext:
+    """One rank's ferret_ep context: buffers exported to, and mapped from, every
+    peer.  Collective: every rank of `group` constructs it with the same sizes.
+    The 64-byte CUDA IPC handles are exchanged with all_gather_object."""
+
+    def __init__(self, E: int, topk: int, max_tokens: int, K: int, N: int, flags: int,
+                 placement: torch.Tensor | None, group=None):
+        from ._lib import check, lib
+        self.L = lib()
+        self.group = group
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        hb = int(self.L.ferret_ep_handle_bytes())
+        handle = (ctypes.c_uint8 * hb)()
+        ctx = ctypes.c_void_p()
+        pl = None
+        if placement is not None:
+            self._placement = (ctypes.c_int32 * E)(*[int(x) for x in placement.tolist()])
+            pl = ctypes.cast(self._placement, ctypes.c_void_p)
+        check(self.L.ferret_ep_init(rank, world, E, topk, max_tokens, K, N, flags, pl,
+                                    ctypes.cast(handle, ctypes.c_void_p), ctypes.byref(ctx)),
+              "ferret_ep_init")
+        self.ctx = ctx
+        self.max_tokens = max_tokens
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        buf = (ctypes.c_uint8 * (hb * world)).from_buffer_copy(b"".join(handles))
+        check(self.L.ferret_ep_connect(ctx, ctypes.cast(buf, ctypes.c_void_p)), "ferret_ep_connect")
+        if world > 1:
+            dist.barrier(group)
+
+    def forward(self, hidden, topk_ids, W, Ws, out):
+        from ._lib import check
+        T = topk_ids.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"T={T} exceeds the context's max_tokens={self.max_tokens}")
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        check(self.L.ferret_ep_w13_forward(self.ctx, ctypes.c_void_p(hidden.data_ptr()),
+                                           ctypes.c_void_p(topk_ids.data_ptr()), T,
+                                           ctypes.c_void_p(W.data_ptr()),
+                                           ctypes.c_void_p(Ws.data_ptr()),
+                                           ctypes.c_void_p(out.data_ptr()), stream),
+              "ferret_ep_w13_forward")
+        return out
+
+    def close(self):
+        """Collective: waits for this rank's work, meets the peers, frees."""
+        if self.ctx is None:
+            return
+        torch.cuda.synchronize()
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.barrier(self.group)
+        self.L.ferret_ep_destroy(self.ctx)
+        self.ctx = None
+
+
 @dataclass
 class StepTimers:
     """Optional CUDA events recorded around the local GEMM of a step."""
@@ -101,8 +171,9 @@ class ExpertParallelW13:
     GATHER_BYTES = 64 << 20    # dense combine buffer above which "auto" uses a2a
 
     def __init__(self, W_local, Ws_local, E: int, group=None, silu: bool = False,
-                 placement: torch.Tensor | None = None, kernels=None, mode: str = "auto"):
-        if mode not in ("auto", "a2a", "gather"):
+                 placement: torch.Tensor | None = None, kernels=None, mode: str = "auto",
+                 max_tokens: int | None = None):
+        if mode not in ("auto", "a2a", "gather", "p2p"):
             raise ValueError(mode)
         self.mode = mode
         self.group = group
@@ -124,6 +195,17 @@ class ExpertParallelW13:
             inv[placement.long()] = torch.arange(E, dtype=torch.int32)
             self.remap = inv.to(dev)
         self.loc_pattern = torch.arange(self.El, dtype=torch.int32, device=dev).repeat(self.G)
+        self.placement = placement
+        self.max_tokens = max_tokens
+        self.peer = None
+        if mode == "p2p" and not (W_local.is_cuda and isinstance(self.kernels, CudaKernels)):
+            raise ValueError("mode 'p2p' runs the CUDA library on GPU-resident weights")
+
+    def close(self):
+        """Collective: releases the peer-memory context (mode "p2p")."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _a2a(self, out, inp, out_splits=None, in_splits=None):
         if self.G == 1:
@@ -144,11 +226,30 @@ class ExpertParallelW13:
         N = self.W.shape[1]
         n_out = N // 2 if self.silu else N
         mode = self.mode
+        if mode == "p2p":
+            return self._forward_p2p(hidden, topk_ids, timers)
         if mode == "auto":
             mode = "gather" if self.G * T * topk * n_out * 2 <= self.GATHER_BYTES else "a2a"
         if mode == "gather":
             return self._forward_gather(hidden, topk_ids, timers)
         return self._forward_a2a(hidden, topk_ids, timers)
+
+    def _forward_p2p(self, hidden, topk_ids, timers):
+        from ._lib import FERRET_SILU_MUL
+        T, topk = topk_ids.shape
+        K = hidden.shape[1]
+        N = self.W.shape[1]
+        if self.peer is None:
+            self.peer = PeerContext(self.E, topk, self.max_tokens or T, K, N,
+                                    FERRET_SILU_MUL if self.silu else 0, self.placement, self.group)
+        out = torch.empty(T * topk, N // 2 if self.silu else N, dtype=torch.bfloat16,
+                          device=hidden.device)
+        if timers is not None and timers.gemm_start is not None:
+            timers.gemm_start.record()
+        self.peer.forward(hidden.contiguous(), topk_ids.contiguous(), self.W, self.Ws, out)
+        if timers is not None and timers.gemm_end is not None:
+            timers.gemm_end.record()
+        return out
 
     def _remap(self, ids: torch.Tensor) -> torch.Tensor:
         if self.remap is None:

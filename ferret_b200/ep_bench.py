@@ -1,13 +1,15 @@
 """Multi-GPU leg of bench.py: the same global W13 batch run expert-parallel.
 
-Launched by torchrun (one process per GPU, NCCL).  Rank r owns E/G experts
+Launched by torchrun (one process per GPU).  Rank r owns E/G experts
 (contiguous ids, or the balanced placement with --placement balanced) and
-T/G of the tokens; one step = ExpertParallelW13.forward (permute, count
-exchange, bf16 dispatch all_to_all, local permute + FP8 quant + grouped GEMM,
-combine all_to_all).  Strong scaling: the global batch is fixed as G grows.
-Decode-sized batches (the sync-free "gather" exchange) run each step as one
-CUDA graph replay, the NCCL collectives inside the graph; prefill-sized ones
-("a2a", one host sync per step for the splits) run eagerly.
+T/G of the tokens; one step = ExpertParallelW13.forward.  The default
+exchange (--ep-mode p2p) is the library's peer-memory path: own-token FP8
+quantization, device flag barriers, routed FP8 rows pulled from the source
+ranks, grouped GEMM storing its rows into the source ranks' outputs over
+NVLink.  --ep-mode gather / a2a / auto use torch.distributed NCCL collectives
+instead.  Strong scaling: the global batch is fixed as G grows.
+Modes without a host synchronisation (p2p, gather) run each step as one CUDA
+graph replay; "a2a" (one host sync per step for the splits) runs eagerly.
 Timing: CUDA events per step on each rank's stream, 256 MB L2 flush between
 steps, barrier + synchronize around the timed region, max over ranks.
 """
@@ -42,6 +44,7 @@ def run(args, cfg):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    ep = graph = None
     try:
         from . import build
         if local == 0:
@@ -64,9 +67,12 @@ def run(args, cfg):
         W, Ws = data.fp8_weights(El, cfg.N, cfg.K, seed=1000 + rank, device=dev)
         ids = ids_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
         hidden = hidden_g[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
-        ep = ExpertParallelW13(W, Ws, cfg.E, silu=cfg.silu, placement=placement)
+        mode = getattr(args, "ep_mode", "p2p")
+        ep = ExpertParallelW13(W, Ws, cfg.E, silu=cfg.silu, placement=placement, mode=mode)
         n_out = cfg.N // 2 if cfg.silu else cfg.N
-        graphed = ep.G * Tl * cfg.topk * n_out * 2 <= ep.GATHER_BYTES   # sync-free gather mode
+        if mode == "auto":
+            mode = "gather" if ep.G * Tl * cfg.topk * n_out * 2 <= ep.GATHER_BYTES else "a2a"
+        graphed = mode in ("p2p", "gather")      # no host synchronisation inside a step
 
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
         for _ in range(args.warmup):
@@ -178,7 +184,8 @@ def run(args, cfg):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out; bf16 dispatch",
+            "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out; "
+                     + ("fp8 dispatch" if mode == "p2p" else "bf16 dispatch"),
             "data": "synthetic (seeded), random-init weights",
             "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
                        "routed_rows": R_global, "K": cfg.K, "N": cfg.N, "silu": cfg.silu,
@@ -195,11 +202,14 @@ def run(args, cfg):
                     "ms_per_step": round(max_e2e, 4),
                     "h2d_bytes_per_step": (h_hidden.numel() * 2 + h_ids.numel() * 4) * G,
                     "d2h_bytes_per_step": h_out.numel() * 2 * G},
-            "gpu_launches": 4 * K,
+            "gpu_launches": (7 if mode == "p2p" else 4) * K,
+            "ep_mode": mode,
             "cuda_graph": graph is not None,
             "clocks": clk,
         }
     finally:
         graph = None        # a graph holding NCCL work must be released before teardown
         torch.cuda.synchronize()
+        if ep is not None:
+            ep.close()      # collective: peer-memory context (p2p)
         dist.destroy_process_group()

@@ -63,8 +63,10 @@ def moe_permute(topk_ids: torch.Tensor, num_experts: int):
     sorted_rows = torch.empty(T * topk, dtype=torch.int32, device=dev)
     offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
     m_indices = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    ws_bytes = int(lib().ferret_moe_permute_workspace_size(T, topk, num_experts))
+    ws = torch.empty(max(ws_bytes, 4) // 4, dtype=torch.int32, device=dev) if ws_bytes else None
     check(lib().ferret_moe_permute(_ptr(topk_ids), T, topk, num_experts, _ptr(sorted_rows),
-                                   _ptr(offsets), _ptr(m_indices), None, 0, _stream()),
+                                   _ptr(offsets), _ptr(m_indices), _ptr(ws), ws_bytes, _stream()),
           "ferret_moe_permute")
     return sorted_rows, offsets, m_indices
 
@@ -158,6 +160,11 @@ def m_grouped_fp8_gemm_scatter(a, b, out: torch.Tensor, expert_offsets: torch.Te
         "ferret_fp8_grouped_gemm_scatter")
 
 
+# Routed rows above which the W13 path quantizes each token once and gathers
+# the FP8 copies (identical bytes; topk-fold less quantizer arithmetic).
+QUANT_ONCE_ROWS = 8192
+
+
 class W13Buffers:
     """Preallocated intermediates of the fused W13 path for fixed sizes."""
 
@@ -169,6 +176,13 @@ class W13Buffers:
         self.a = torch.empty(R, K, dtype=torch.uint8, device=device)
         self.a_scale = torch.empty(R, K // 128, dtype=torch.float32, device=device)
         self.out = torch.empty(R, N_out, dtype=torch.bfloat16, device=device)
+        ws = int(lib().ferret_moe_permute_workspace_size(T, topk, E))
+        self.perm_ws = torch.empty(ws // 4, dtype=torch.int32, device=device) if ws else None
+        self.perm_ws_bytes = ws
+        self.quant_once = R > QUANT_ONCE_ROWS and topk > 1
+        if self.quant_once:
+            self.q_tok = torch.empty(T, K, dtype=torch.uint8, device=device)
+            self.s_tok = torch.empty(T, K // 128, dtype=torch.float32, device=device)
 
 
 def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
@@ -195,11 +209,20 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
     s = _stream()
     R = T * topk
     check(L.ferret_moe_permute(_ptr(topk_ids), T, topk, E, _ptr(bufs.sorted_rows),
-                               _ptr(bufs.offsets), _ptr(bufs.m_indices), None, 0, s),
+                               _ptr(bufs.offsets), _ptr(bufs.m_indices), _ptr(bufs.perm_ws),
+                               bufs.perm_ws_bytes, s),
           "ferret_moe_permute")
-    check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K,
-                                       _ptr(bufs.a), _ptr(bufs.a_scale), s),
-          "ferret_quant_act_fp8_1x128")
+    if bufs.quant_once:
+        # each token once, then its topk routed copies in expert order
+        check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, None, 1, T, K, _ptr(bufs.q_tok),
+                                           _ptr(bufs.s_tok), s), "ferret_quant_act_fp8_1x128")
+        check(L.ferret_fp8_gather_rows(_ptr(bufs.q_tok), _ptr(bufs.s_tok), T,
+                                       _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
+                                       _ptr(bufs.a_scale), s), "ferret_fp8_gather_rows")
+    else:
+        check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K,
+                                           _ptr(bufs.a), _ptr(bufs.a_scale), s),
+              "ferret_quant_act_fp8_1x128")
     flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
     check(L.ferret_fp8_grouped_gemm_nt_contiguous(
         _ptr(bufs.a), _ptr(bufs.a_scale), _ptr(W), _ptr(W_scale), _ptr(bufs.out), None,

@@ -83,8 +83,13 @@ FERRET_API int ferret_selftest_wait_timeout(unsigned long long timeout_ns, void*
  *                 expert, ascending inside an expert; -1 past the valid count
  * expert_offsets: int32 [E+1] exclusive prefix of the per-expert counts
  * m_indices:      int32 [T*topk] expert of each sorted row (-1 in the tail)
- * No workspace is needed (pass NULL, 0).  Limits: E <= 1024.
+ * workspace: NULL (one CTA sorts all ids -- the fastest form for decode
+ *   sizes) or ferret_moe_permute_workspace_size(T, topk, E) bytes, 4-byte
+ *   aligned, which lets large batches (more than 4096 ids) sort in chunks
+ *   over many CTAs.  The result is identical either way.  A size of 0 means
+ *   no workspace is used at that size.  Limits: E <= 1024.
  */
+FERRET_API size_t ferret_moe_permute_workspace_size(int T, int topk, int E);
 FERRET_API int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int E, int32_t* sorted_rows,
                        int32_t* expert_offsets, int32_t* m_indices, void* workspace,
                        size_t ws_bytes, void* stream);
@@ -106,6 +111,19 @@ FERRET_API int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int 
 FERRET_API int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows, const int32_t* gather_rows,
                                           int gather_div, int R, int K, void* a_fp8,
                                           float* a_scale, void* stream);
+
+/*
+ * Row gather of quantized rows (no reference counterpart; an alternative to
+ * the gathered quantizer above with identical output): out row r = row
+ * rows[r] / div of q_fp8 [src_rows, K] / q_scale [src_rows, K/128]
+ * (negative -> zero row and scale; a source row >= src_rows is treated like
+ * a negative one and reported as device status 4).  Quantizing T token rows
+ * once and gathering their T*topk routed copies saves topk-fold quantizer
+ * arithmetic at prefill sizes.  Limits: K % 128 == 0; 16-byte aligned rows.
+ */
+FERRET_API int ferret_fp8_gather_rows(const void* q_fp8, const float* q_scale, int src_rows,
+                                      const int32_t* rows, int div, int R, int K, void* out_fp8,
+                                      float* out_scale, void* stream);
 
 /*
  * FP8 block-scaled grouped GEMM, contiguous layout, W13 (gate+up).
@@ -211,6 +229,51 @@ FERRET_API int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
                                    const int32_t* sorted_rows, const int32_t* expert_offsets,
                                    void* out_bf16, int T, int topk, int N, int K, int E, int flags,
                                    void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * Expert-parallel FP8 W13 over NVLink peer memory, one process per GPU.
+ * No reference counterpart: the reference has no multi-GPU implementation of
+ * this path.  The entry points keep its shim conventions
+ * (tests/compare_decode_linear.py:110-128: raw device pointers and ints,
+ * caller-owned buffers, stream as void*, int status) and the per-rank result
+ * equals the single-GPU ferret_fp8_grouped_gemm_nt_contiguous output for the
+ * rank's own (token, slot) pairs.
+ *
+ * Setup, on every rank with its GPU current:
+ *   ferret_ep_init(rank, world, E, topk, max_tokens, K, N, flags, placement,
+ *                  handle, &ctx)  -- allocates this rank's buffers and writes
+ *                  its ferret_ep_handle_bytes()-byte export handle;
+ *   all-gather the handles in rank order over any bootstrap;
+ *   ferret_ep_connect(ctx, handles) -- maps every peer's buffers.
+ * placement: NULL (rank r owns experts [r*E/world, (r+1)*E/world)) or a host
+ * array of E distinct expert ids in owner order (slot i on rank i/(E/world)).
+ * flags: FERRET_SILU_MUL and the token-tile bits, as for the grouped GEMM.
+ *
+ * Step (every rank, same T <= max_tokens, collective over the ranks):
+ *   ferret_ep_w13_forward(ctx, hidden [T, K] bf16, topk_ids [T, topk] int32
+ *       (global expert ids; ids outside [0, E) give zero rows),
+ *       T, w_fp8 [E/world, N, K] e4m3 and w_scale [E/world, N/128, K/128] f32
+ *       of this rank's experts in placement order, out [T*topk, N or N/2]
+ *       bf16 in (token, slot) order or NULL to leave the result in
+ *       ferret_ep_output_buffer(ctx), stream).
+ * It enqueues kernels only (no host synchronisation, no allocation), so a
+ * step can be captured in a CUDA graph.  A peer that does not arrive within
+ * the wait timeout makes the step record a device timeout
+ * (ferret_last_device_status: 1 | site << 8, site 20 or 21); the context is
+ * then out of step and must be destroyed.
+ * ferret_ep_destroy: only after every rank's last step has completed.
+ */
+typedef struct ferret_ep ferret_ep;
+FERRET_API size_t ferret_ep_handle_bytes(void);
+FERRET_API int ferret_ep_init(int rank, int world, int num_experts, int topk, int max_tokens, int K,
+                              int N, int flags, const int32_t* placement, void* handle_out,
+                              ferret_ep** ctx);
+FERRET_API int ferret_ep_connect(ferret_ep* ctx, const void* all_handles);
+FERRET_API int ferret_ep_w13_forward(ferret_ep* ctx, const void* hidden_bf16, const int32_t* topk_ids,
+                                     int T, const void* w_fp8, const float* w_scale, void* out_bf16,
+                                     void* stream);
+FERRET_API void* ferret_ep_output_buffer(ferret_ep* ctx);
+FERRET_API int ferret_ep_destroy(ferret_ep* ctx);
 
 #ifdef __cplusplus
 }

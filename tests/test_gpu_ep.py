@@ -1,5 +1,9 @@
-"""Expert parallelism on 2 GPUs (NCCL): every (token, slot) output equals the
-single-GPU W13 path on the same inputs, bit for bit.  Skips on a 1-GPU box."""
+"""Expert parallelism on 2 GPUs: every (token, slot) output equals the
+single-GPU W13 path on the same inputs, bit for bit -- for the NCCL exchange
+modes ("a2a", "gather") and for the peer-memory mode ("p2p", the library's
+ferret_ep_* entry points), eagerly and replayed from a CUDA graph.  A second
+test checks that a p2p step whose peer never arrives ends with a bounded
+device timeout instead of a hang.  Skips on a 1-GPU box."""
 import os
 import socket
 
@@ -18,7 +22,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _init(rank, world, port):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -28,6 +32,19 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
+    return dev
+
+
+def _all_true(ok, dev):
+    import torch.distributed as dist
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    dev = _init(rank, world, port)
     try:
         from ferret_b200 import data, ops
         from ferret_b200.ep import ExpertParallelW13, balanced_placement
@@ -35,27 +52,54 @@ def _worker(rank, world, port, q):
         W, Ws = data.fp8_weights(E, N, K, device=dev)
         hidden = data.activations(T, K).to(dev)
         ids = data.routing(T, E, topk, "zipf").to(dev)
-        # single-GPU result on every rank, (token, slot) order
-        out, rows, _ = ops.fp8_moe_w13(hidden, ids, W, Ws)
-        ref = torch.empty_like(out)
-        ref[rows.long()] = out
-        cases = [(p, m) for p in (None, balanced_placement(torch.bincount(ids.reshape(-1).cpu(), minlength=E), world))
-                 for m in ("a2a", "gather")]
-        for placement, mode in cases:
+        ids[3, 1] = -1            # a dropped pair: zero row in every mode
+        ids[T - 1, 0] = E + 5
+        refs = {}
+        for silu in (False, True):
+            out, rows, _ = ops.fp8_moe_w13(hidden, ids, W, Ws, silu=silu)
+            ref = torch.zeros(T * topk, out.shape[1], dtype=out.dtype, device=dev)
+            live = rows >= 0
+            ref[rows[live].long()] = out[live]
+            refs[silu] = ref
+        bal = balanced_placement(torch.bincount(ids.reshape(-1).clamp(0, E - 1).cpu(), minlength=E), world)
+        cases = [(p, m, False) for p in (None, bal) for m in ("a2a", "gather", "p2p")]
+        cases += [(None, "p2p", True), (bal, "p2p", True)]
+        El, Tl = E // world, T // world
+        h_loc = hidden[rank * Tl:(rank + 1) * Tl].contiguous()
+        i_loc = ids[rank * Tl:(rank + 1) * Tl].contiguous()
+        results = []
+        for placement, mode, silu in cases:
             table = placement if placement is not None else torch.arange(E)
-            El, Tl = E // world, T // world
             mine = table[rank * El:(rank + 1) * El].long().to(dev)
             ep = ExpertParallelW13(W[mine].contiguous(), Ws[mine].contiguous(), E, placement=placement,
-                                   mode=mode)
-            got = ep.forward(hidden[rank * Tl:(rank + 1) * Tl].contiguous(),
-                             ids[rank * Tl:(rank + 1) * Tl].contiguous())
-            torch.cuda.synchronize()
-            want = ref[rank * Tl * topk:(rank + 1) * Tl * topk]
-            ok = torch.equal(got.view(torch.int16), want.view(torch.int16))
-            flag = torch.tensor([1 if ok else 0], device=dev)
-            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-            if rank == 0:
-                q.put(bool(flag.item()))
+                                   mode=mode, silu=silu, max_tokens=2 * Tl)
+            want = refs[silu][rank * Tl * topk:(rank + 1) * Tl * topk]
+            steps = 3 if mode == "p2p" else 1      # several epochs through one context
+            ok = True
+            for _ in range(steps):
+                got = ep.forward(h_loc, i_loc)
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
+            if mode == "p2p" and silu:
+                # the same step replayed from a CUDA graph
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(g, stream=side):
+                        got_g = ep.forward(h_loc, i_loc)
+                torch.cuda.current_stream().wait_stream(side)
+                for _ in range(2):
+                    got_g.zero_()
+                    g.replay()
+                    torch.cuda.synchronize()
+                    ok = ok and torch.equal(got_g.view(torch.int16), want.view(torch.int16))
+                del g
+            ok = ok and ops.last_device_status() == 0
+            ep.close()
+            results.append(_all_true(ok, dev))
+        if rank == 0:
+            q.put(results)
     except Exception as e:
         q.put(f"rank {rank}: {type(e).__name__}: {e}")
         raise
@@ -63,17 +107,72 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_ep_two_gpus_matches_single_gpu(cuda_device):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run(worker, world=2, timeout=300):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in range(4)]
+    res = q.get(timeout=timeout)
     for p in procs:
         p.join(timeout=120)
-    assert all(r is True for r in results), results
-    assert all(p.exitcode == 0 for p in procs)
+    return res, [p.exitcode for p in procs]
+
+
+def test_ep_two_gpus_matches_single_gpu(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res, codes = _run(_worker)
+    assert isinstance(res, list) and len(res) == 8 and all(res), res
+    assert all(c == 0 for c in codes)
+
+
+def _timeout_worker(rank, world, port, q):
+    """Step 1 runs on both ranks; in step 2 rank 1 stays on the host (alive,
+    its buffers mapped), so rank 0's ready barrier must give up after the
+    wait timeout and report it through the status word."""
+    import torch.distributed as dist
+    dev = _init(rank, world, port)
+    try:
+        from ferret_b200 import data, ops
+        from ferret_b200.ep import ExpertParallelW13
+        E, N, K, T, topk = 8, 256, 256, 8, 2
+        W, Ws = data.fp8_weights(E, N, K, device=dev)
+        El, Tl = E // world, T // world
+        hidden = data.activations(T, K)[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
+        ids = data.routing(T, E, topk, "uniform")[rank * Tl:(rank + 1) * Tl].contiguous().to(dev)
+        ep = ExpertParallelW13(W[rank * El:(rank + 1) * El].contiguous(),
+                               Ws[rank * El:(rank + 1) * El].contiguous(), E, mode="p2p")
+        ep.forward(hidden, ids)
+        torch.cuda.synchronize()
+        ok1 = ops.last_device_status() == 0
+        dist.barrier()
+        status = 0
+        if rank == 0:
+            ops.set_wait_timeout(0.2)
+            ep.forward(hidden, ids)          # rank 1 never arrives
+            torch.cuda.synchronize()
+            status = ops.last_device_status()
+            ops.set_wait_timeout(2.0)
+        dist.barrier()                       # rank 1 keeps its buffers until rank 0 is done
+        ep.close()
+        if rank == 0:
+            q.put((ok1, status))
+    except Exception as e:
+        q.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_p2p_missing_peer_times_out(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res, codes = _run(_timeout_worker)
+    assert isinstance(res, tuple), res
+    ok1, status = res
+    assert ok1
+    # DEV_TIMEOUT (1) from the ready barrier (site 20) or the done barrier (21)
+    assert status & 0xFF == 1 and (status >> 8) in (20, 21), hex(status)
+    assert all(c == 0 for c in codes)

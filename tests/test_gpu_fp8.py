@@ -53,6 +53,53 @@ def test_permute_bit_exact(ops, T, topk, E, lo, hi):
     assert np.array_equal(d_mi.cpu().numpy(), mi)
 
 
+@pytest.mark.parametrize("T,topk,E,lo,hi", [
+    (513, 8, 256, 0, 256),          # 4104 ids: two chunks
+    (4099, 3, 7, -1, 8),            # ragged chunks, dropped ids at both ends of the range
+    (32768, 8, 32, 0, 32),          # the all-rank sort of 8-way EP prefill (1024 ids/expert)
+    (262144, 8, 256, 0, 256),       # 2M ids: the 256-chunk limit
+])
+def test_permute_chunked_matches_single_cta(ops, T, topk, E, lo, hi):
+    """The multi-CTA (workspace) form and the one-CTA form give the same bits,
+    and both match the oracle."""
+    import ctypes
+    from ferret_b200._lib import lib
+    rng = np.random.default_rng(T * 3 + E)
+    ids_np = rng.integers(lo, hi, size=(T, topk)).astype(np.int32)
+    ids = torch.from_numpy(ids_np).cuda()
+    L = lib()
+    ws_bytes = int(L.ferret_moe_permute_workspace_size(T, topk, E))
+    assert ws_bytes > 0
+    outs = []
+    for ws in (torch.empty(ws_bytes // 4, dtype=torch.int32, device="cuda"), None):
+        r = torch.full((T * topk,), 7, dtype=torch.int32, device="cuda")
+        o = torch.full((E + 1,), 7, dtype=torch.int32, device="cuda")
+        m = torch.full((T * topk,), 7, dtype=torch.int32, device="cuda")
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = L.ferret_moe_permute(ctypes.c_void_p(ids.data_ptr()), T, topk, E,
+                                  ctypes.c_void_p(r.data_ptr()), ctypes.c_void_p(o.data_ptr()),
+                                  ctypes.c_void_p(m.data_ptr()),
+                                  None if ws is None else ctypes.c_void_p(ws.data_ptr()),
+                                  0 if ws is None else ws_bytes, stream)
+        assert rc == 0
+        outs.append((r.cpu().numpy(), o.cpu().numpy(), m.cpu().numpy()))
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    if T * topk <= 300000:
+        rows, offs, mi = O.moe_permute(ids_np, E)
+        assert np.array_equal(outs[0][0], rows)
+        assert np.array_equal(outs[0][1], offs)
+        assert np.array_equal(outs[0][2], mi)
+    else:   # stable-sort properties at the largest size
+        r, o, m = outs[0]
+        flat = ids_np.reshape(-1)
+        assert np.array_equal(o, np.concatenate([[0], np.cumsum(np.bincount(flat, minlength=E))]))
+        assert np.array_equal(flat[r], m)
+        for e in (0, E // 2, E - 1):
+            seg = r[o[e]:o[e + 1]]
+            assert np.all(np.diff(seg) > 0)
+
+
 # ---------------------------------------------------------------- quantization
 
 @pytest.mark.parametrize("R,K", [(1, 128), (37, 512), (1024, 7168)])
@@ -76,6 +123,32 @@ def test_quant_gather_bit_exact(ops):
     qr, sr = O.quant_act_fp8_1x128(u16(x), rows.numpy(), topk)
     assert np.array_equal(u8(q), qr)
     assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+
+
+@pytest.mark.parametrize("T,topk,K", [(5, 3, 256), (1024, 8, 7168)])
+def test_gather_rows_equals_gathered_quant(ops, T, topk, K):
+    """Quantize-once + ferret_fp8_gather_rows gives the bytes of the gathered
+    quantizer, including zero rows for negative indices."""
+    import ctypes
+    from ferret_b200._lib import lib
+    g = torch.Generator().manual_seed(T + K)
+    x = torch.randn(T, K, generator=g).to(torch.bfloat16).cuda()
+    rows = torch.randperm(T * topk, generator=g).to(torch.int32)
+    rows[::7] = -1
+    rows = rows.cuda()
+    qa, sa = ops.per_token_cast_to_fp8(x, rows, topk)
+    qt, st = ops.per_token_cast_to_fp8(x)
+    R = rows.numel()
+    qb = torch.full((R, K), 0x55, dtype=torch.uint8, device="cuda")
+    sb = torch.full((R, K // 128), 3.0, dtype=torch.float32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib().ferret_fp8_gather_rows(ctypes.c_void_p(qt.data_ptr()), ctypes.c_void_p(st.data_ptr()), T,
+                                      ctypes.c_void_p(rows.data_ptr()), topk, R, K,
+                                      ctypes.c_void_p(qb.data_ptr()), ctypes.c_void_p(sb.data_ptr()),
+                                      stream)
+    assert rc == 0
+    assert torch.equal(qa.view(torch.uint8), qb)
+    assert torch.equal(sa.view(torch.int32), sb.view(torch.int32))
 
 
 def test_quant_matches_torch_cuda_published_algorithm(ops):
