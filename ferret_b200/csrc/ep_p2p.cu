@@ -12,9 +12,10 @@
 //                   exported buffer                               (local)
 //   2. ready      : copy own top-k ids into the exported buffer, zero the
 //                   output rows of invalid ids, raise "ready(epoch)" on every
-//                   peer, wait for every peer's; then read all G*T*topk ids
-//                   from the peers and map them to local experts (-1 when the
-//                   expert lives elsewhere)                       (peer loads)
+//                   peer, wait for every peer's (one CTA); then a grid-wide
+//                   kernel reads all G*T*topk ids from the peers and maps them
+//                   to local experts (-1 when the expert lives elsewhere)
+//                                                                 (peer loads)
 //   3. permute    : stable counting sort of the G*T*topk pairs by local expert
 //   4. gather     : expert-sorted FP8 rows + scales pulled from the source
 //                   ranks into the local A operand                (peer loads)
@@ -67,6 +68,7 @@ struct EpDev {
     uint8_t* a;                         // [world*T*topk, K] gathered e4m3 rows
     float* a_s;                         // [world*T*topk, K/128]
     uint32_t* epoch;                    // device step counter
+    int* failed;                        // set by a ready barrier that ran out (this step)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -121,26 +123,39 @@ __global__ void __launch_bounds__(kSignalThreads, 1)
         __threadfence_system();     // ids, rows above and the quantized rows before the flag
     }
     __syncthreads();
-    const uint32_t epoch = s_epoch;
+    const bool ok = ep_barrier(d, 0, s_epoch, ctl, SITE_EP_READY);
+    if (tid == 0) *d.failed = ok ? 0 : 1;
+}
+
+// Every rank's ids (peer loads, many CTAs) -> local expert per pair, or -1.
+// After a failed ready barrier no pair is routed here: the rest of the step
+// is empty and touches no peer memory.
+__global__ void __launch_bounds__(kGatherThreads)
+    ep_ids_kernel(const EpDev d) {
+    const int own = d.T * d.topk;
     const int total = d.world * own;
-    if (!ep_barrier(d, 0, epoch, ctl, SITE_EP_READY)) {
-        // out of step: no pair is routed here, so the rest of the step is empty
-        for (int i = tid; i < total; i += kSignalThreads) d.all_ids[i] = -1;
-        return;
-    }
-    for (int i = tid; i < total; i += kSignalThreads) {
-        const int g = i / own;
-        const int id = __ldcv(d.ids_peers[g] + (i - g * own));
-        d.all_ids[i] = (id >= 0 && id < d.E) ? d.remap[id] : -1;
+    const bool failed = *d.failed != 0;
+    for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < total; i += gridDim.x * kGatherThreads) {
+        int v = -1;
+        if (!failed) {
+            const int g = i / own;
+            const int id = __ldcv(d.ids_peers[g] + (i - g * own));
+            v = (id >= 0 && id < d.E) ? d.remap[id] : -1;
+        }
+        d.all_ids[i] = v;
     }
 }
 
-// Pull the expert-sorted rows: one warp per row, 16-byte peer loads.
+// Pull the expert-sorted rows: one warp per row, 16-byte peer loads, all of
+// a lane's loads for the row (up to 16: K <= 16384) issued before any store so
+// the NVLink latency is paid once per row, not once per load.
 __global__ void __launch_bounds__(kGatherThreads)
     ep_gather_kernel(const EpDev d) {
+    constexpr int kMaxVec = 16;
     const int rows = d.offsets[d.El];
     const int lane = threadIdx.x & 31;
     const int nk = d.K >> 7;
+    const int vec = d.K >> 4;                 // 16-byte words per row
     const int own = d.T * d.topk;
     const int warps = gridDim.x * (kGatherThreads / 32);
     for (int r = blockIdx.x * (kGatherThreads / 32) + (threadIdx.x >> 5); r < rows; r += warps) {
@@ -148,10 +163,32 @@ __global__ void __launch_bounds__(kGatherThreads)
         const int g = src / own;
         const int t = (src - g * own) / d.topk;
         const uint4* q = reinterpret_cast<const uint4*>(d.q_peers[g] + (size_t)t * d.K);
-        uint4* dst = reinterpret_cast<uint4*>(d.a + (size_t)r * d.K);
-        for (int c = lane; c < (d.K >> 4); c += 32) dst[c] = __ldcv(q + c);
         const float* s = d.s_peers[g] + (size_t)t * nk;
-        for (int c = lane; c < nk; c += 32) d.a_s[(size_t)r * nk + c] = __ldcv(s + c);
+        uint4* dst = reinterpret_cast<uint4*>(d.a + (size_t)r * d.K);
+        float sc[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {         // nk <= 128
+            const int c = lane + 32 * j;
+            if (c < nk) sc[j] = __ldcv(s + c);
+        }
+        for (int base = 0; base < vec; base += 32 * kMaxVec) {   // 8 KB of the row per pass
+            uint4 v[kMaxVec];
+#pragma unroll
+            for (int j = 0; j < kMaxVec; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) v[j] = __ldcv(q + c);
+            }
+#pragma unroll
+            for (int j = 0; j < kMaxVec; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) dst[c] = v[j];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = lane + 32 * j;
+            if (c < nk) d.a_s[(size_t)r * nk + c] = sc[j];
+        }
     }
 }
 
@@ -224,7 +261,7 @@ extern "C" int ferret_ep_init(int rank, int world, int num_experts, int topk, in
     if (num_experts <= 0 || num_experts % world || num_experts / world > 1024) return FERRET_ERR_SHAPE;
     if (topk <= 0 || max_tokens <= 0 || K <= 0 || K % 128 || N <= 0 || N % 128 || (pair && N % 256))
         return FERRET_ERR_SHAPE;
-    if (K / 128 > 128 || (long long)(num_experts / world) * N >= (1ll << 31)) return FERRET_ERR_SHAPE;
+    if (K > 16384 || (long long)(num_experts / world) * N >= (1ll << 31)) return FERRET_ERR_SHAPE;
     const long long pairs = (long long)world * max_tokens * topk;
     if (pairs >= (1ll << 30) || pairs * K >= (1ll << 40)) return FERRET_ERR_SHAPE;
     DeviceInfo* info = nullptr;
@@ -423,11 +460,18 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     d.a = c->a;
     d.a_s = c->a_s;
     d.epoch = c->epoch;
+    d.failed = reinterpret_cast<int*>(c->epoch + 1);
     const DevCtl ctl = make_ctl(info);
 
     // 2. publish ids, meet the peers, read every rank's ids
     ep_ready_kernel<<<1, kSignalThreads, 0, s>>>(d, topk_ids, ctl);
     if ((rc = launch_status()) != FERRET_OK) return rc;
+    {
+        const int want = (pairs + kGatherThreads - 1) / kGatherThreads;
+        const int grid = want < info->num_sms * 4 ? want : info->num_sms * 4;
+        ep_ids_kernel<<<grid, kGatherThreads, 0, s>>>(d);
+        if ((rc = launch_status()) != FERRET_OK) return rc;
+    }
     // 3. local expert order of all pairs
     rc = ferret_moe_permute(c->all_ids, c->world * T, c->topk, c->El, c->sorted, c->offsets,
                             c->m_idx, c->perm_ws, c->perm_ws_bytes, stream);

@@ -128,7 +128,19 @@ class PeerContext:
         if world > 1:
             dist.barrier(group)
 
-    def forward(self, hidden, topk_ids, W, Ws, out):
+    def output_view(self, rows: int, cols: int) -> torch.Tensor:
+        """The context's exported output buffer as a bf16 [rows, cols] tensor
+        (no copy; rewritten by the next step)."""
+        ptr = self.L.ferret_ep_output_buffer(self.ctx)
+
+        class _Buf:
+            __cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<i2",
+                                        "data": (ptr, False), "version": 3, "strides": None,
+                                        "stream": None}
+        return torch.as_tensor(_Buf(), device=torch.cuda.current_device()).view(torch.bfloat16)
+
+    def forward(self, hidden, topk_ids, W, Ws, out=None):
+        """One step; `out` None leaves the rows in the context's buffer."""
         from ._lib import check
         T = topk_ids.shape[0]
         if T > self.max_tokens:
@@ -138,7 +150,8 @@ class PeerContext:
                                            ctypes.c_void_p(topk_ids.data_ptr()), T,
                                            ctypes.c_void_p(W.data_ptr()),
                                            ctypes.c_void_p(Ws.data_ptr()),
-                                           ctypes.c_void_p(out.data_ptr()), stream),
+                                           None if out is None else ctypes.c_void_p(out.data_ptr()),
+                                           stream),
               "ferret_ep_w13_forward")
         return out
 
@@ -221,7 +234,11 @@ class ExpertParallelW13:
                 timers: StepTimers | None = None) -> torch.Tensor:
         """hidden bf16 [T, K], topk_ids int32 [T, topk] (global expert ids) ->
         bf16 [T*topk, N or N/2] in (token, slot) order; pairs with an invalid
-        expert id get zero rows.  Every rank passes the same T."""
+        expert id get zero rows.  Every rank passes the same T.  In mode "p2p"
+        the result is a view of the context's output buffer, valid until the
+        next forward (work queued on the current stream in between reads it
+        safely: peers write the next step's rows only after this rank's next
+        step has started)."""
         T, topk = topk_ids.shape
         N = self.W.shape[1]
         n_out = N // 2 if self.silu else N
@@ -242,14 +259,13 @@ class ExpertParallelW13:
         if self.peer is None:
             self.peer = PeerContext(self.E, topk, self.max_tokens or T, K, N,
                                     FERRET_SILU_MUL if self.silu else 0, self.placement, self.group)
-        out = torch.empty(T * topk, N // 2 if self.silu else N, dtype=torch.bfloat16,
-                          device=hidden.device)
         if timers is not None and timers.gemm_start is not None:
             timers.gemm_start.record()
-        self.peer.forward(hidden.contiguous(), topk_ids.contiguous(), self.W, self.Ws, out)
+        self.peer.forward(hidden.contiguous(), topk_ids.contiguous(), self.W, self.Ws)
         if timers is not None and timers.gemm_end is not None:
             timers.gemm_end.record()
-        return out
+        # zero-copy: the rows stay in the exported buffer until the next step
+        return self.peer.output_view(T * topk, N // 2 if self.silu else N)
 
     def _remap(self, ids: torch.Tensor) -> torch.Tensor:
         if self.remap is None:

@@ -163,6 +163,13 @@ def run(args, cfg):
         R_global = int(flat.numel())
         flops = 2.0 * R_global * cfg.N * cfg.K
 
+        if mode == "p2p":
+            # quant, ready, ids, permute (1, or count/scan/scatter), row gather, GEMM, done
+            from ._lib import lib
+            chunked = lib().ferret_moe_permute_workspace_size(G * Tl, cfg.topk, El) > 0
+            launches = 6 + (3 if chunked else 1)
+        else:
+            launches = 4
         max_step = _max(step_ms, dev)
         max_gemm = _max(gemm_ms, dev)
         max_e2e = _max(e2e_ms, dev)
@@ -202,7 +209,7 @@ def run(args, cfg):
                     "ms_per_step": round(max_e2e, 4),
                     "h2d_bytes_per_step": (h_hidden.numel() * 2 + h_ids.numel() * 4) * G,
                     "d2h_bytes_per_step": h_out.numel() * 2 * G},
-            "gpu_launches": (7 if mode == "p2p" else 4) * K,
+            "gpu_launches": launches * K,
             "ep_mode": mode,
             "cuda_graph": graph is not None,
             "clocks": clk,
