@@ -10,11 +10,12 @@
 //
 //   1. quant_act  : own hidden [T, K] -> e4m3 rows + 1x128 scales in the
 //                   exported buffer                               (local)
-//   2. ready      : copy own top-k ids into the exported buffer, zero the
-//                   output rows of invalid ids, raise "ready(epoch)" on every
-//                   peer, wait for every peer's (one CTA); then a grid-wide
-//                   kernel reads all G*T*topk ids from the peers and maps them
-//                   to local experts (-1 when the expert lives elsewhere)
+//   2. publish    : copy own top-k ids into the exported buffer, zero the
+//                   output rows of invalid ids                    (local)
+//      ready      : raise "ready(epoch)" on every peer, wait for every
+//                   peer's (one CTA)
+//      ids        : read all G*T*topk ids from the peers and map them to
+//                   local experts (-1 when the expert lives elsewhere)
 //                                                                 (peer loads)
 //   3. permute    : stable counting sort of the G*T*topk pairs by local expert
 //   4. gather     : expert-sorted FP8 rows + scales pulled from the source
@@ -45,7 +46,6 @@ namespace ferret {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kSignalThreads = 512;
 constexpr int kGatherThreads = 256;
 constexpr int SITE_EP_READY = 20, SITE_EP_DONE = 21;
 
@@ -102,29 +102,34 @@ __device__ bool ep_barrier(const EpDev& d, int slot_base, uint32_t epoch, DevCtl
     return __syncthreads_and(ok) != 0;
 }
 
-__global__ void __launch_bounds__(kSignalThreads, 1)
-    ep_ready_kernel(const EpDev d, const int32_t* __restrict__ topk_ids, DevCtl ctl) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// This rank's ids into the exported buffer; output rows of invalid ids are
+// zeroed here (no rank's GEMM writes them).  Grid-wide, one id per thread.
+__global__ void __launch_bounds__(kGatherThreads)
+    ep_publish_kernel(const EpDev d, const int32_t* __restrict__ topk_ids) {
     const int own = d.T * d.topk;
-    __shared__ uint32_t s_epoch;
-    // own ids into the exported buffer; output rows of invalid ids are zero
-    for (int i = tid; i < own; i += kSignalThreads) d.ids_sym[i] = topk_ids[i];
-    for (int i = warp; i < own; i += kSignalThreads / 32) {
+    for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < own; i += gridDim.x * kGatherThreads) {
         const int id = topk_ids[i];
+        d.ids_sym[i] = id;
         if (id < 0 || id >= d.E) {
             uint4* row = reinterpret_cast<uint4*>(d.out_sym + (size_t)i * d.n_out);
-            for (int c = lane; c < d.n_out / 8; c += 32) row[c] = make_uint4(0, 0, 0, 0);
+            for (int c = 0; c < d.n_out / 8; ++c) row[c] = make_uint4(0, 0, 0, 0);
         }
     }
-    __syncthreads();
-    if (tid == 0) {
+}
+
+// One CTA: advance the step counter, raise "ready" on every rank (after a
+// system fence: the quantized rows, ids and zeroed rows written by the
+// kernels before this one are visible first), wait for every rank's.
+__global__ void __launch_bounds__(32, 1) ep_ready_kernel(const EpDev d, DevCtl ctl) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) {
         s_epoch = *d.epoch + 1u;
         *d.epoch = s_epoch;
-        __threadfence_system();     // ids, rows above and the quantized rows before the flag
+        __threadfence_system();
     }
     __syncthreads();
     const bool ok = ep_barrier(d, 0, s_epoch, ctl, SITE_EP_READY);
-    if (tid == 0) *d.failed = ok ? 0 : 1;
+    if (threadIdx.x == 0) *d.failed = ok ? 0 : 1;
 }
 
 // Every rank's ids (peer loads, many CTAs) -> local expert per pair, or -1.
@@ -464,7 +469,13 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     const DevCtl ctl = make_ctl(info);
 
     // 2. publish ids, meet the peers, read every rank's ids
-    ep_ready_kernel<<<1, kSignalThreads, 0, s>>>(d, topk_ids, ctl);
+    {
+        const int want = (own + kGatherThreads - 1) / kGatherThreads;
+        const int grid = want < info->num_sms * 4 ? want : info->num_sms * 4;
+        ep_publish_kernel<<<grid, kGatherThreads, 0, s>>>(d, topk_ids);
+        if ((rc = launch_status()) != FERRET_OK) return rc;
+    }
+    ep_ready_kernel<<<1, 32, 0, s>>>(d, ctl);
     if ((rc = launch_status()) != FERRET_OK) return rc;
     {
         const int want = (pairs + kGatherThreads - 1) / kGatherThreads;

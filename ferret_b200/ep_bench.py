@@ -164,10 +164,10 @@ def run(args, cfg):
         flops = 2.0 * R_global * cfg.N * cfg.K
 
         if mode == "p2p":
-            # quant, ready, ids, permute (1, or count/scan/scatter), row gather, GEMM, done
+            # quant, publish, ready, ids, permute (1, or count/scan/scatter), row gather, GEMM, done
             from ._lib import lib
             chunked = lib().ferret_moe_permute_workspace_size(G * Tl, cfg.topk, El) > 0
-            launches = 6 + (3 if chunked else 1)
+            launches = 7 + (3 if chunked else 1)
         else:
             launches = 4
         max_step = _max(step_ms, dev)
