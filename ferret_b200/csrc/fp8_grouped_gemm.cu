@@ -491,11 +491,16 @@ constexpr int kPfEpi = 256;
 constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
 constexpr int kPfMaxStages = 6;
 
+// Per epilogue warp: a 32-row x 32-column bf16 staging block (rows padded to
+// 80 bytes: conflict-free 16-byte writes) and the 32 rows' output pointers.
+constexpr int kPfStgRow = 80;
+constexpr int kPfStgWarp = 32 * kPfStgRow + 32 * 8;
+
 struct PfLayout {
-    int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
+    int stages_off, segs_off, segc_off, mts_off, part_off, stg_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline PfLayout pf_layout(int stages, int E) {
+__host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
     PfLayout L;
     int o = 0;
     L.stages_off = o;
@@ -508,7 +513,9 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E) {
     o += 4 * (E + 1);
     L.part_off = o;
     o += 4 * (kPfThreads + 1);
-    o = (o + 7) & ~7;
+    o = (o + 15) & ~15;
+    L.stg_off = o;
+    if (staged) o += kPfStgWarp * (kPfEpi / 32);
     L.bar_off = o;
     o += 8 * (2 * kPfMaxStages + 2 * 2 + 2);
     L.misc_off = o;
@@ -517,7 +524,10 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E) {
     return L;
 }
 
-template <bool PAIR>
+// STAGED: output rows written through shared memory, 64 contiguous bytes of
+// 8 rows per store instruction -- used when rows go to other GPUs, where
+// 16-byte writes scattered over 32 rows make poor NVLink transactions.
+template <bool PAIR, bool STAGED>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
@@ -527,7 +537,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7;
     const int nbc = N >> 8;                        // 256-row weight tiles
-    const PfLayout L = pf_layout(NS, E);
+    const PfLayout L = pf_layout(NS, E, STAGED);
     int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
     int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
@@ -655,6 +665,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint8_t* stg = smem + L.stg_off + (warp - 2) * kPfStgWarp;
+        __nv_bfloat16** rowp = reinterpret_cast<__nv_bfloat16**>(stg + 32 * kPfStgRow);
         RingPos ra;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int e, row0, rows, nb;
@@ -701,42 +713,85 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 orow = __ldg(args.out_rows + row0 + r);
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
-            if (live && orow >= 0) {
-                __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
-                if (PAIR) {
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+            if (!STAGED) {
+                if (live && orow >= 0) {
+                    __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
+                    if (PAIR) {
+                        uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
 #pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 pk;
-                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+                        for (int c = 0; c < 64; c += 8) {
+                            uint4 pk;
+                            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b = __floats2bfloat162_rn(
-                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
-                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
-                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                            for (int j = 0; j < 4; ++j) {
+                                const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                    silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                    silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                                pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                            }
+                            dst[c >> 3] = pk;
                         }
-                        dst[c >> 3] = pk;
-                    }
-                } else {
-                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
-                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+                    } else {
+                        uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                        uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
 #pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 p0, p1;
-                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
-                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+                        for (int c = 0; c < 64; c += 8) {
+                            uint4 p0, p1;
+                            uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                            uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
-                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
-                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
-                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                            for (int j = 0; j < 4; ++j) {
+                                const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                                const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                                w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                                w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                            }
+                            d0[c >> 3] = p0;
+                            d1[c >> 3] = p1;
                         }
-                        d0[c >> 3] = p0;
-                        d1[c >> 3] = p1;
                     }
                 }
+                continue;
+            }
+            // Staged: every store instruction writes 64 contiguous bytes of 8
+            // rows instead of 16 bytes of 32 rows.
+            rowp[lane] = (live && orow >= 0) ? out_row_ptr(args, orow, ldo) : nullptr;
+#pragma unroll
+            for (int k = 0; k < (PAIR ? 2 : 4); ++k) {
+                // chunk k: 32 columns of this thread's row
+                uint4 pk[4];
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    uint32_t* pw = reinterpret_cast<uint32_t*>(&pk[v]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int c = (PAIR ? k * 32 : (k & 1) * 32) + v * 8 + 2 * j;
+                        __nv_bfloat162 b;
+                        if (PAIR)
+                            b = __floats2bfloat162_rn(silu_mul(acc0[c], acc1[c]),
+                                                      silu_mul(acc0[c + 1], acc1[c + 1]));
+                        else if (k < 2)
+                            b = __floats2bfloat162_rn(acc0[c], acc0[c + 1]);
+                        else
+                            b = __floats2bfloat162_rn(acc1[c], acc1[c + 1]);
+                        pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                    }
+                }
+                uint4* srow = reinterpret_cast<uint4*>(stg + lane * kPfStgRow);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) srow[v] = pk[v];
+                __syncwarp();
+                const int col = PAIR ? nb * 128 + h * 64 + k * 32
+                                     : nb * 256 + (k >> 1) * 128 + h * 64 + (k & 1) * 32;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int idx = i * 32 + lane, row = idx >> 2, part = idx & 3;
+                    __nv_bfloat16* o = rowp[row];
+                    if (o)
+                        reinterpret_cast<uint4*>(o + col)[part] =
+                            *reinterpret_cast<const uint4*>(stg + row * kPfStgRow + part * 16);
+                }
+                __syncwarp();
             }
         }
     }
@@ -750,8 +805,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
 }
 
-template <bool PAIR>
-int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+template <bool PAIR, bool STAGED>
+int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                        const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
                        int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
     CUtensorMap tm_w, tm_a;
@@ -761,10 +816,10 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
     rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
     if (rc != FERRET_OK) return rc;
     const int budget = info->max_smem_optin - 1024;
-    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E).total) / kPfStage);
+    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E, STAGED).total) / kPfStage);
     if (stages < 2) return FERRET_ERR_SHAPE;
-    const int smem = pf_layout(stages, E).total + 1024;
-    auto kern = fp8_w13_prefill_kernel<PAIR>;
+    const int smem = pf_layout(stages, E, STAGED).total + 1024;
+    auto kern = fp8_w13_prefill_kernel<PAIR, STAGED>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
         cudaGetLastError();
         return FERRET_ERR_CUDA;
@@ -787,6 +842,16 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
     g.ctl = make_ctl(info);
     kern<<<info->num_sms, kPfThreads, smem, stream>>>(tm_w, tm_a, g);
     return launch_status();
+}
+
+template <bool PAIR>
+int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
+    return om.peers ? launch_fp8_prefill_t<PAIR, true>(info, a, a_scale, w, w_scale, out, seg,
+                                                       seg_pairs, M, N, K, E, stream, om)
+                    : launch_fp8_prefill_t<PAIR, false>(info, a, a_scale, w, w_scale, out, seg,
+                                                        seg_pairs, M, N, K, E, stream, om);
 }
 
 int pick_tile(int M, int E, int flags, bool pair) {

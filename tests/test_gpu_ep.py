@@ -64,16 +64,32 @@ def _worker(rank, world, port, q):
         bal = balanced_placement(torch.bincount(ids.reshape(-1).clamp(0, E - 1).cpu(), minlength=E), world)
         cases = [(p, m, False) for p in (None, bal) for m in ("a2a", "gather", "p2p")]
         cases += [(None, "p2p", True), (bal, "p2p", True)]
-        El, Tl = E // world, T // world
-        h_loc = hidden[rank * Tl:(rank + 1) * Tl].contiguous()
-        i_loc = ids[rank * Tl:(rank + 1) * Tl].contiguous()
+        cases += [("big", "p2p", False), ("big", "p2p", True)]   # prefill kernel, peer stores
+        # a batch large enough (> 48 rows per local expert) for the prefill kernel
+        Tb = 1024
+        hidden_b = data.activations(Tb, K, seed=11).to(dev)
+        ids_b = data.routing(Tb, E, topk, "zipf").to(dev)
+        refs_b = {}
+        for silu in (False, True):
+            out, rows, _ = ops.fp8_moe_w13(hidden_b, ids_b, W, Ws, silu=silu)
+            ref = torch.zeros(Tb * topk, out.shape[1], dtype=out.dtype, device=dev)
+            ref[rows.long()] = out
+            refs_b[silu] = ref
+        El = E // world
         results = []
         for placement, mode, silu in cases:
+            big = isinstance(placement, str)
+            if big:
+                placement = None
+            Tn, hid_n, ids_n, refs_n = (Tb, hidden_b, ids_b, refs_b) if big else (T, hidden, ids, refs)
+            Tl = Tn // world
+            h_loc = hid_n[rank * Tl:(rank + 1) * Tl].contiguous()
+            i_loc = ids_n[rank * Tl:(rank + 1) * Tl].contiguous()
             table = placement if placement is not None else torch.arange(E)
             mine = table[rank * El:(rank + 1) * El].long().to(dev)
             ep = ExpertParallelW13(W[mine].contiguous(), Ws[mine].contiguous(), E, placement=placement,
                                    mode=mode, silu=silu, max_tokens=2 * Tl)
-            want = refs[silu][rank * Tl * topk:(rank + 1) * Tl * topk]
+            want = refs_n[silu][rank * Tl * topk:(rank + 1) * Tl * topk]
             steps = 3 if mode == "p2p" else 1      # several epochs through one context
             ok = True
             for _ in range(steps):
@@ -124,7 +140,7 @@ def test_ep_two_gpus_matches_single_gpu(cuda_device):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     res, codes = _run(_worker)
-    assert isinstance(res, list) and len(res) == 8 and all(res), res
+    assert isinstance(res, list) and len(res) == 10 and all(res), res
     assert all(c == 0 for c in codes)
 
 
