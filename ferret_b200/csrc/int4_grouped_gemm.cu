@@ -51,7 +51,8 @@ constexpr int kRawS = 128 * 4 * 2;     // scales: 4 groups x 128 n bf16
 constexpr int kBlob = kRawW + kRawS;   // 9216 B per 128 x 128 weight block
 constexpr int kQCols = 64;             // TMEM columns of one dequantized 128x128 tile
 
-enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_QE = 3, I4_QF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7 };
+enum : int { I4_EMPTY = 1, I4_FULL = 2, I4_QE = 3, I4_QF = 4, I4_TE = 5, I4_TF = 6, I4_DRAIN = 7,
+             I4_EPI = 8 };
 
 struct Int4Args {
     const uint8_t* blob;          // [E][N/128][K/128] x kBlob
@@ -60,6 +61,12 @@ struct Int4Args {
     __nv_bfloat16* out;
     int T, topk, N, K, E, R;
     int stages;
+    // split-K (splits > 1): unit u = tile * splits + s covers K blocks
+    // [s*nk/splits, (s+1)*nk/splits); fp32 partials go to part[u][col][128],
+    // cnt[tile] counts finished units and the last one reduces in s order
+    int splits;
+    float* part;
+    int* cnt;
     DevCtl ctl;
 };
 
@@ -91,7 +98,7 @@ __host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int E
     o += 4 * (kI4Threads + 1);
     o = (o + 7) & ~7;
     L.bar_off = o;
-    o += 8 * (2 * kI4MaxStages + 2 * kI4MaxQ + 2 * kI4MaxAcc + 1);
+    o += 8 * (2 * kI4MaxStages + 2 * kI4MaxQ + 2 * kI4MaxAcc + 2);
     L.misc_off = o;
     o += 16;
     L.total = o;
@@ -168,6 +175,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     auto tf_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + a); };
     auto te_bar = [&](int a) { return bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + kI4MaxAcc + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * kI4MaxStages + 2 * kI4MaxQ + 2 * kI4MaxAcc);
+    const uint32_t epi_bar = drain_bar + 8u;      // epilogue rendezvous (split-K), bounded
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
     uint8_t* raw = smem + L.raw_off;
@@ -187,6 +195,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             mbar_init(te_bar(a), kI4EpiThreads);
         }
         mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kI4EpiThreads);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -209,7 +218,8 @@ __global__ void __launch_bounds__(kI4Threads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t q_base = tmem_base + C::kAccCols;          // dequantized-tile slots
-    const int total = mt_start[E] * nbc;
+    const int S = args.splits;
+    const int total = mt_start[E] * nbc * S;                  // work units
     const size_t blob_nb = (size_t)(K >> 7) * kBlob;          // bytes per (e, n-block)
 
     if (warp == 0) {
@@ -221,12 +231,13 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             int it = 0;
             RingPos rp;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const int t = u / S, sp = u - t * S;
                 int e, row0, rows, nb;
                 i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
                 const uint8_t* wg = args.blob + ((size_t)e * (N >> 7) + nb) * blob_nb;
                 const uint8_t* wu = args.blob + ((size_t)e * (N >> 7) + (N >> 8) + nb) * blob_nb;
-                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                for (int kb = sp * nk / S; kb < (sp + 1) * nk / S; ++kb, ++it, rp.advance(NS)) {
                     const int s = rp.slot;
                     if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, I4_EMPTY)) {
                         ok = false;
@@ -251,11 +262,13 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             constexpr uint32_t idesc = make_idesc(128, NT, 1, 1);
             RingPos rs, rq, ra;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ra.advance(C::kAcc)) {
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ra.advance(C::kAcc)) {
+                const int sp = u % S;
+                const int kb0 = sp * nk / S, kb1 = (sp + 1) * nk / S;
                 const int a = ra.slot;
                 if (!mbar_wait(te_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, I4_TE)) break;
                 const uint32_t d_acc = tmem_base + a * C::kCols;
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS)) {
+                for (int kb = kb0; kb < kb1; ++kb, rs.advance(NS)) {
                     const int s = rs.slot;
                     RingPos qw[C::kW];
                     qw[0] = rq;
@@ -279,7 +292,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                     const uint32_t bt = raw_base + s * C::kStage + C::kW * kBlob;
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
-                        const uint32_t acc = (kb | ks) ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || ks) ? 1u : 0u;
                         const uint64_t bdesc =
                             sdesc_k_sw128(bt + (ks >> 2) * NT * 128 + (ks & 3) * 32);
 #pragma unroll
@@ -307,8 +320,22 @@ __global__ void __launch_bounds__(kI4Threads, 1)
         RingPos rs, rq;
         int job = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            for (int kb = 0; kb < nk && ok; ++kb, rs.advance(NS)) {
+        // Software pipeline: a job's TMEM stores are left in flight while the
+        // next job's words are fetched and dequantized; only then does the
+        // warp wait for them and hand the slot to the MMA (pend).
+        int pend = -1;
+        auto release_pending = [&]() {
+            if (pend >= 0) {
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(qf_bar(pend));
+                pend = -1;
+            }
+        };
+        for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+            const int sp = u % S;
+            for (int kb = sp * nk / S; kb < (sp + 1) * nk / S && ok; ++kb, rs.advance(NS)) {
 #pragma unroll
                 for (int w = 0; w < C::kW; ++w, ++job, rq.advance(NQ)) {
                     if ((job & (kDqGroups - 1)) != g) continue;
@@ -338,21 +365,30 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                             r[4 * i + 2] = v.z;
                             r[4 * i + 3] = v.w;
                         }
+                        if (h == 0) release_pending();     // the previous job's stores are done
                         tmem_st32(col + h * 32, r);
                     }
-                    tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(qf_bar(rq.slot));
+                    pend = rq.slot;
                 }
             }
         }
+        release_pending();
     } else {
         // ================= epilogue =================
         const int q = warp & 3;
         const int ldo = PAIR ? (N >> 1) : N;
+        const int et = tid - kEpiWarp0 * 32;             // 0..127 = weight row of the tile
+        __shared__ int s_last;
+        uint32_t epi_phase = 0;
+        auto epi_sync = [&]() -> bool {                  // bounded, abort-aware rendezvous
+            mbar_arrive(epi_bar);
+            const bool ok = mbar_wait(epi_bar, epi_phase & 1u, abort_flag, args.ctl, I4_EPI);
+            ++epi_phase;
+            return __all_sync(0xffffffffu, ok);
+        };
         RingPos ra;
-        for (int t = blockIdx.x; t < total; t += gridDim.x, ra.advance(C::kAcc)) {
+        for (int u = blockIdx.x; u < total; u += gridDim.x, ra.advance(C::kAcc)) {
+            const int t = u / S;
             int e, row0, rows, nb;
             i4_decode_tile<NT>(t, nbc, E, mt_start, args.offsets, e, row0, rows, nb);
             const int a = ra.slot;
@@ -361,6 +397,55 @@ __global__ void __launch_bounds__(kI4Threads, 1)
             tc_fence_after();
             const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * C::kCols;
             const int ncol = nb * 128 + q * 32 + lane;
+            if (S > 1) {
+                // this unit's fp32 partial, [col][row] so a warp writes 128 contiguous bytes
+                float* pu = args.part + (size_t)u * C::kCols * 128 + et;
+#pragma unroll
+                for (int c = 0; c < C::kCols; c += 8) {
+                    uint32_t r[8];
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+                                   "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                                 : "r"(tb + c));
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) pu[(size_t)(c + j) * 128] = __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                mbar_arrive(te_bar(a));
+                __threadfence();
+                if (!epi_sync()) break;
+                if (et == 0) s_last = (atomicAdd(args.cnt + t, 1) == S - 1);
+                if (!epi_sync()) break;
+                if (!s_last) continue;
+                __threadfence();
+                // last unit of the tile: sum the S partials in split order
+                const float* pt = args.part + (size_t)t * S * C::kCols * 128 + et;
+#pragma unroll
+                for (int c = 0; c < NT; c += 8) {
+                    float g[8], v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) g[j] = v[j] = 0.0f;
+                    for (int s2 = 0; s2 < S; ++s2) {
+                        const float* ps = pt + (size_t)s2 * C::kCols * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            g[j] += __ldcg(ps + (size_t)(c + j) * 128);
+                            if (PAIR) v[j] += __ldcg(ps + (size_t)(NT + c + j) * 128);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (c + j < rows) {
+                            const int orow = __ldg(args.sorted_rows + row0 + c + j);
+                            const float val = PAIR ? silu_mul(g[j], v[j]) : g[j];
+                            args.out[(size_t)orow * ldo + ncol] = __float2bfloat16_rn(val);
+                        }
+                    }
+                }
+                if (et == 0) args.cnt[t] = 0;     // ready for the next launch
+                continue;
+            }
             // 8 token columns at a time: few live registers
 #pragma unroll
             for (int c = 0; c < NT; c += 8) {
@@ -437,9 +522,12 @@ __global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint1
 
 // Expert-sorted activation rows: out[r] = hidden[rows[r] / topk]
 // (zero row for a negative entry or a token >= T, the latter reported).
+// Also clears the ncnt split-K tile counters for the GEMM that follows.
 __global__ void gather_rows_kernel(const uint4* __restrict__ hidden, const int32_t* __restrict__ rows,
                                    int topk, int T, int R, int K, uint4* __restrict__ out,
-                                   DevCtl ctl) {
+                                   int* __restrict__ cnt, int ncnt, DevCtl ctl) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x)
+        cnt[i] = 0;
     const int per_row = K >> 3;                                // 16-byte chunks
     const size_t total = (size_t)R * per_row;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -458,7 +546,8 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ hidden, const int32
 template <int NT, bool PAIR>
 int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blob,
                 const int32_t* sorted_rows, const int32_t* offsets, void* out, int T, int topk,
-                int N, int K, int E, int R, cudaStream_t stream) {
+                int N, int K, int E, int R, cudaStream_t stream, uint8_t* split_ws,
+                size_t split_bytes) {
     using C = I4Cfg<NT, PAIR>;
     CUtensorMap tm_a;
     // gathered activations [R, K] bf16, box = 64 K values x NT rows
@@ -466,6 +555,9 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
                           64, NT, true);
     if (rc != FERRET_OK) return rc;
     static_assert(C::kQ >= C::kW * 2, "too few TMEM tile slots");
+    // each dequant group may hold a finished slot while it waits for its next
+    // one: the MMA can always drain in order only with more slots than groups
+    static_assert(C::kQ >= kDqGroups + 1, "too few TMEM tile slots for the dequant pipeline");
     const int budget = info->max_smem_optin - 1024;
     const I4Layout l0 = i4_layout(C::kStage, 0, E);
     const int stages = std::min(kI4MaxStages, (budget - l0.total) / C::kStage);
@@ -490,6 +582,25 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
     a.R = R;
     a.stages = stages;
     a.ctl = make_ctl(info);
+    // Split K when the tiles cannot fill the SMs (decode with a handful of
+    // tokens): at most the bound on tiles, floor(SMs / tiles) splits of at
+    // least 4 K blocks, if the workspace holds the partials.
+    a.splits = 1;
+    a.part = nullptr;
+    a.cnt = nullptr;
+    const int nbc = PAIR ? N / 256 : N / 128;
+    const long long tiles_up = ((long long)std::min(R, E) + R / NT) * nbc;
+    if (split_ws && tiles_up > 0) {
+        // (the counters, tiles_up ints at split_ws, were cleared by the row gather)
+        const int S = (int)std::min<long long>(info->num_sms / tiles_up, (K / 128) / 4);
+        const size_t part_bytes = (size_t)tiles_up * S * C::kCols * 128 * sizeof(float);
+        const size_t cnt_bytes = (size_t)tiles_up * sizeof(int);
+        if (S >= 2 && part_bytes + cnt_bytes <= split_bytes) {
+            a.splits = S;
+            a.cnt = reinterpret_cast<int*>(split_ws);
+            a.part = reinterpret_cast<float*>(split_ws + ((cnt_bytes + 255) & ~size_t(255)));
+        }
+    }
     kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_a, a);
     return launch_status();
 }
@@ -504,9 +615,15 @@ extern "C" size_t ferret_int4_blob_bytes(int E, int K, int N) {
     return (size_t)E * (N / 128) * (K / 128) * kBlob;
 }
 
+// Routed rows up to which the workspace also holds split-K partials (decode
+// with a handful of tokens), and the space reserved for them.
+constexpr int kSplitMaxRows = 64;
+constexpr size_t kSplitBytes = (size_t)9 << 20;
+
 extern "C" size_t ferret_int4_moe_w13_workspace_size(int T, int topk, int K) {
     if (T < 0 || topk <= 0 || K <= 0) return 0;
-    return (size_t)T * topk * K * 2;
+    const size_t rows = (size_t)T * topk * K * 2;
+    return T * topk <= kSplitMaxRows ? ((rows + 255) & ~size_t(255)) + kSplitBytes : rows;
 }
 
 extern "C" int ferret_int4_repack_w13(const int32_t* w_raw, const void* w_scale_bf16, void* w_blob,
@@ -549,26 +666,40 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
     if (rc != FERRET_OK) return rc;
     cudaStream_t s = as_stream(stream);
     const int R = T * topk;
-    {
-        const size_t chunks = (size_t)R * (K / 8);
-        const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)info->num_sms * 8);
-        gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(hidden_bf16), sorted_rows,
-                                                topk, T, R, K, static_cast<uint4*>(workspace),
-                                                make_ctl(info));
-        if ((rc = launch_status()) != FERRET_OK) return rc;
-    }
     const uint8_t* blob = static_cast<const uint8_t*>(w_blob);
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
     if (nt == 0) {
         const int avg = (R + E - 1) / E;
         nt = avg <= 4 ? 8 : avg <= 12 ? 16 : 32;
     }
+    // the workspace tail past the gathered rows holds split-K counters + partials
+    const size_t rows_bytes = ((size_t)R * K * 2 + 255) & ~size_t(255);
+    uint8_t* split_ws = nullptr;
+    size_t split_bytes = 0;
+    int ncnt = 0;
+    if (R <= kSplitMaxRows && ws_bytes > rows_bytes) {
+        split_ws = static_cast<uint8_t*>(workspace) + rows_bytes;
+        split_bytes = ws_bytes - rows_bytes;
+        const long long tiles_up = ((long long)std::min(R, E) + R / std::max(nt, 1)) * (pair ? N / 256 : N / 128);
+        ncnt = (int)std::min<long long>(tiles_up, (long long)(split_bytes / sizeof(int)));
+    }
+    {
+        const size_t chunks = (size_t)R * (K / 8);
+        const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)info->num_sms * 8);
+        gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(hidden_bf16), sorted_rows,
+                                                topk, T, R, K, static_cast<uint4*>(workspace),
+                                                reinterpret_cast<int*>(split_ws), ncnt,
+                                                make_ctl(info));
+        if ((rc = launch_status()) != FERRET_OK) return rc;
+    }
 #define FERRET_I4_CASE(NT_)                                                                        \
     case NT_:                                                                                      \
         return pair ? launch_int4<NT_, true>(info, workspace, blob, sorted_rows, expert_offsets,   \
-                                             out_bf16, T, topk, N, K, E, R, s)                     \
+                                             out_bf16, T, topk, N, K, E, R, s, split_ws,           \
+                                             split_bytes)                                          \
                     : launch_int4<NT_, false>(info, workspace, blob, sorted_rows, expert_offsets,  \
-                                              out_bf16, T, topk, N, K, E, R, s);
+                                              out_bf16, T, topk, N, K, E, R, s, split_ws,          \
+                                              split_bytes);
     switch (nt) {
         FERRET_I4_CASE(8)
         FERRET_I4_CASE(16)

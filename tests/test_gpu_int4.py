@@ -93,6 +93,23 @@ def test_int4_vs_oracle(ops, T, E, K, N, topk, silu, tile):
     assert not got[~valid].any()
 
 
+@pytest.mark.parametrize("T,E,K,N,topk,silu", [
+    (1, 384, 7168, 512, 8, True),        # the reference's TP8 T=1 shape
+    (2, 16, 2048, 256, 4, False),
+    (4, 32, 4096, 512, 8, True),
+])
+def test_int4_split_k_vs_oracle(ops, T, E, K, N, topk, silu):
+    """Few tokens: the kernel splits K over the SMs and the last unit of each
+    tile reduces the fp32 partials.  Two calls in a row check that the tile
+    counters are left ready for the next launch."""
+    h, rq, sc, ids = inputs(T * 7 + E, T, E, K, N, topk, hscale=0.01)
+    ref = O.int4_w13_fast(h, rq, sc, ids, silu=silu)
+    for _ in range(2):
+        got = run(ops, h, rq, sc, ids, silu)
+        err = O.rel_err(got, ref)
+        assert err["nan"] == 0 and err["max_rel"] < TOL and err["max_abs"] < 0.012, err
+
+
 def test_int4_reference_golden_kimi_shape(ops):
     """The reference's own oracle output at its own shape (H=7168, 2I=512, top-8)."""
     sys.path.insert(0, GOLD)
