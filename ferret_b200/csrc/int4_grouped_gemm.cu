@@ -555,9 +555,10 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
                           64, NT, true);
     if (rc != FERRET_OK) return rc;
     static_assert(C::kQ >= C::kW * 2, "too few TMEM tile slots");
-    // each dequant group may hold a finished slot while it waits for its next
-    // one: the MMA can always drain in order only with more slots than groups
-    static_assert(C::kQ >= kDqGroups + 1, "too few TMEM tile slots for the dequant pipeline");
+    // Each dequant group may hold a finished slot while it waits for a free one
+    // for its next job; the slot it waits for must belong to an MMA step that
+    // needs none of the held jobs (an MMA step takes kW consecutive jobs).
+    static_assert(C::kQ >= kDqGroups + C::kW, "too few TMEM tile slots for the dequant pipeline");
     const int budget = info->max_smem_optin - 1024;
     const I4Layout l0 = i4_layout(C::kStage, 0, E);
     const int stages = std::min(kI4MaxStages, (budget - l0.total) / C::kStage);
