@@ -48,6 +48,10 @@ def parse_args():
     ap.add_argument("--ep-mode", choices=["p2p", "gather", "a2a", "auto"], default="p2p",
                     help="N>1 exchange: p2p = peer-memory kernels (library ferret_ep_*); "
                          "gather / a2a / auto = torch.distributed NCCL collectives")
+    ap.add_argument("--suite", choices=["", "v007-configs"], default="",
+                    help="v007-configs: the reference kernel's own 8 benchmark shapes "
+                         "(E=32 experts, gate_up and down, 1-16 rows per expert); with --impl "
+                         "reference, the reference's own GPU kernel compiled unmodified")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="profiling aid: run N bare GEMM launches and exit")
     return ap.parse_args()
@@ -523,8 +527,100 @@ def run_reference(args, cfg):
     }
 
 
+# ---------------------------------------------------------------------------
+# the reference kernel's own benchmark shapes
+# (tasks/fp8-group-gemm-dsv3-decode.yaml:45-86, v007_dsv3_decode_verified_105.cu:473-478)
+# ---------------------------------------------------------------------------
+
+V007_CONFIGS = [("gate_up_M1", 1, 32, 7168, 4096), ("gate_up_M4", 4, 32, 7168, 4096),
+                ("gate_up_M8", 8, 32, 7168, 4096), ("gate_up_M16", 16, 32, 7168, 4096),
+                ("down_M1", 1, 32, 2048, 7168), ("down_M4", 4, 32, 2048, 7168),
+                ("down_M8", 8, 32, 2048, 7168), ("down_M16", 16, 32, 2048, 7168)]
+
+
+def run_v007_suite(args):
+    """Our grouped GEMM through the DeepGEMM-style call (m_indices, segments
+    derived on the device) at the reference kernel's 8 shapes: random e4m3
+    operands (NaN codes skipped), scales in [0.5, 1), median of 100 launches,
+    256 MB L2 flush before each."""
+    import torch
+    from ferret_b200 import build, ops
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(42)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def e4m3_bytes(*shape):
+        b = torch.randint(0, 254, shape, generator=g, device=dev, dtype=torch.int32)
+        return (b + (b >= 0x7F).int()).to(torch.uint8)
+
+    res, us, res_tile, us_tile = {}, {}, {}, {}
+    for name, mpe, E, K, N in V007_CONFIGS:
+        M = mpe * E
+        A, W = e4m3_bytes(M, K), e4m3_bytes(E, N, K)
+        As = torch.rand(M, K // 128, generator=g, device=dev) * 0.5 + 0.5
+        Ws = torch.rand(E, N // 128, K // 128, generator=g, device=dev) * 0.5 + 0.5
+        mi = (torch.arange(M, device=dev) // mpe).to(torch.int32)
+        # the work the reference kernel does: every 128-row tile takes the
+        # expert of its first row (v007:162,286), so only 1-4 experts stream
+        mi_tile = mi[(torch.arange(M, device=dev) // 128) * 128].contiguous()
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        for m_ind, rd, ud in ((mi, res, us), (mi_tile, res_tile, us_tile)):
+            run = lambda: ops.m_grouped_fp8_gemm_nt_contiguous((A, As), (W, Ws), out, m_ind)
+            for _ in range(20):
+                run()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(100):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                run()
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            times.sort()
+            med = times[50]
+            rd[name] = round(2.0 * M * N * K / (med * 1e-3) / 1e12, 4)
+            ud[name] = round(med * 1e3, 2)
+    if ops.last_device_status() != 0:
+        raise RuntimeError("device status error")
+    return {"suite": "v007-configs", "impl": "ours", "unit": "TFLOPS", "results": res, "us": us,
+            "results_tile_expert": res_tile, "us_tile_expert": us_tile,
+            "timing": "median of 100, 256 MB flush before each, CUDA events",
+            "numerics": "exact fp32 block scales, per-row experts; *_tile_expert: the same call "
+                        "with m_indices set to each 128-row tile's first expert (the work the "
+                        "reference kernel does)"}
+
+
+def run_v007_suite_reference(args):
+    """The reference's own kernel and benchmark main (v007, compiled unmodified
+    into oracle/_ref by `make -C oracle ref`)."""
+    import re
+    import subprocess
+    exe = os.path.join(ROOT, "oracle", "_ref", "v007_bench")
+    if not os.path.exists(exe):
+        return {"suite": "v007-configs", "impl": "reference",
+                "unavailable": "oracle/_ref/v007_bench not built (needs the reference tree)"}
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    m = re.search(r"KERNEL_RESULT (\{.*?\})", r.stdout)
+    if r.returncode != 0 or not m:
+        return {"suite": "v007-configs", "impl": "reference",
+                "unavailable": f"v007_bench exited {r.returncode}"}
+    per_us = dict(re.findall(r"(\w+): [0-9.]+ TFLOPS, ([0-9.]+) us", r.stderr))
+    return {"suite": "v007-configs", "impl": "reference", "unit": "TFLOPS",
+            "results": json.loads(m.group(1)), "us": {k: float(v) for k, v in per_us.items()},
+            "timing": "its own: median of 100, 128 MB flush before each, CUDA events",
+            "numerics": "UE8M0-rounded scales, first-row-of-tile experts (its own check: 32 rows)"}
+
+
 def main():
     args = parse_args()
+    if args.suite == "v007-configs":
+        res = run_v007_suite_reference(args) if args.impl == "reference" else run_v007_suite(args)
+        print(json.dumps(res), flush=True)
+        return
     from ferret_b200.data import CONFIGS
     cfg = CONFIGS[args.workload]
     if args.impl == "reference":
