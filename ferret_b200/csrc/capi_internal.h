@@ -50,11 +50,21 @@ struct OutMap {
     int peer_rows = 0;
 };
 
+// Workspace for split-K of the swap-AB kernel: tile counters (zeroed before
+// the launch) and fp32 partials; part == nullptr disables splitting.
+struct SplitWs {
+    int* cnt = nullptr;
+    float* part = nullptr;
+    size_t bytes = 0;
+    int smax = 1;
+};
+
 // FP8 grouped GEMM launch shared by the entry points: picks the prefill kernel
 // or the swap-AB token tile from rows_hint (expected rows holding data) and E.
 int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                  const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
-                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om);
+                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om,
+                 const SplitWs& sw = SplitWs{});
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -45,6 +45,8 @@ enum : int {
     SITE_EMPTY = 1, SITE_FULL = 2, SITE_TEMPTY = 3, SITE_TFULL = 4, SITE_DRAIN = 5, SITE_EPI = 6
 };
 
+constexpr int kABox = 16;         // token rows per activation TMA box (the MMA N granule)
+
 struct GemmArgs {
     const float* a_scale;
     const float* w_scale;
@@ -57,6 +59,15 @@ struct GemmArgs {
     int peer_rows;
     int M, N, K, E;
     int stages;
+    // split-K for launches with fewer tiles than SMs (swap-AB kernel): the
+    // kernel picks S <= splits_max from the actual tile count so that the
+    // fp32 partials part[unit][col][128] fit part_bytes; cnt[tile] (zeroed
+    // before the launch) finds the last unit of a tile, which reduces in
+    // split order.  splits_max <= 1 disables it.
+    int splits_max;
+    float* part;
+    int* cnt;
+    size_t part_bytes;
     DevCtl ctl;
 };
 
@@ -216,7 +227,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int total = mt_start[E] * nbc;
+    const int tiles = mt_start[E] * nbc;
+    // split-K when the tiles cannot fill the SMs (every CTA derives the same S)
+    int S = 1;
+    if (args.splits_max > 1 && tiles > 0 && 2 * tiles <= (int)gridDim.x) {
+        S = min((int)gridDim.x / tiles, min(args.splits_max, nk));
+        const size_t unit_bytes = (size_t)C::kCols * 128 * sizeof(float);
+        while (S > 1 && (size_t)tiles * S * unit_bytes > args.part_bytes) --S;
+    }
+    const int total = tiles * S;                  // work units: (tile, K split)
 
     if (warp == 0) {
         // ================= TMA producer =================
@@ -227,13 +246,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t pol_a = policy_evict_last();
             int it = 0;
             RingPos rp;
-            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            for (int u = blockIdx.x; u < total; u += gridDim.x) {
+                const int t = u / S, sp = u - t * S;
                 int e, row0, rows, nb;
                 decode_tile<NT>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int nl = (rows + kABox - 1) & ~(kABox - 1);   // live token rows, 16-row granule
                 const int wrow = e * N + nb * 128;
                 const int wrow_up = e * N + (N >> 1) + nb * 128;
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                for (int kb = sp * nk / S; kb < (sp + 1) * nk / S; ++kb, ++it, rp.advance(NS)) {
                     const int s = rp.slot;
                     if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl,
                                    SITE_EMPTY)) {
@@ -241,10 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t dst = stage_base + s * C::kStage;
-                    mbar_expect_tx(full_bar(s), C::kStage);
+                    mbar_expect_tx(full_bar(s), C::kW * kWTile + nl * 128);
                     tma_load_2d_hint(dst, &tm_w, kb * 128, wrow, full_bar(s), pol_w);
                     if (PAIR) tma_load_2d_hint(dst + kWTile, &tm_w, kb * 128, wrow_up, full_bar(s), pol_w);
-                    tma_load_2d_hint(dst + C::kW * kWTile, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    for (int b = 0; b < nl; b += kABox)
+                        tma_load_2d_hint(dst + C::kW * kWTile + b * 128, &tm_a, kb * 128, row0 + b,
+                                         full_bar(s), pol_a);
                 }
                 if (!ok) break;
             }
@@ -255,11 +278,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ================= MMA issuer =================
         if (elect_one()) {
-            constexpr uint32_t idesc = make_idesc(128, NT, 0, 0);
             RingPos rs, ra;
-            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            for (int u = blockIdx.x; u < total; u += gridDim.x) {
+                const int t = u / S, sp = u - t * S;
+                int e, row0, rows, nb;
+                decode_tile<NT>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                // MMA N = the tile's live token rows rounded up to 16
+                const uint32_t idesc = make_idesc(128, (rows + kABox - 1) & ~(kABox - 1), 0, 0);
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(C::kAcc)) {
+                for (int kb = sp * nk / S; kb < (sp + 1) * nk / S; ++kb, rs.advance(NS), ra.advance(C::kAcc)) {
                     const int s = rs.slot, a = ra.slot;
                     if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl,
                                    SITE_TEMPTY) ||
@@ -302,12 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++epi_phase;
             return __all_sync(0xffffffffu, ok);
         };
-        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        __shared__ int s_last;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const int t = u / S, sp = u - t * S;
+            const int kb0 = sp * nk / S, kb1 = (sp + 1) * nk / S;
             int e, row0, rows, nb;
             decode_tile<NT>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const int nl = (rows + kABox - 1) & ~(kABox - 1);
             // stage this tile's scales: a_sc[kb][j], w_sc[g][kb]
             if (!epi_sync()) break;
-            for (int i = et; i < NT * nk; i += kEpiThreads) {
+            for (int i = et; i < nl * nk; i += kEpiThreads) {
                 const int j = i / nk, kb = i - j * nk;
                 a_sc[kb * NT + j] = (j < rows) ? __ldg(args.a_scale + (size_t)(row0 + j) * nk + kb) : 0.0f;
             }
@@ -326,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < (PAIR ? NT : 1); ++j) acc_u[j] = 0.0f;
 
             bool ok = true;
-            for (int kb = 0; kb < nk; ++kb, ++ai) {
+            for (int kb = kb0; kb < kb1; ++kb, ++ai) {
                 const int a = ai % C::kAcc;
                 ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(a), (ai / C::kAcc) & 1, abort_flag,
                                                        args.ctl, SITE_TFULL));
@@ -338,21 +369,54 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float* asc = a_sc + kb * NT;
 #pragma unroll
                 for (int c = 0; c < NT; c += 16) {
-                    float v[16], u[16];
+                    if (c >= nl) break;                  // columns past the tile's MMA N
+                    float v[16], uu[16];
                     tmem_ld16(tb + c, v);
-                    if (PAIR) tmem_ld16(tb + NT + c, u);
+                    if (PAIR) tmem_ld16(tb + NT + c, uu);
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float sa = asc[c + j];
                         acc_g[c + j] = fmaf(v[j], sa * ws, acc_g[c + j]);
-                        if (PAIR) acc_u[c + j] = fmaf(u[j], sa * wsu, acc_u[c + j]);
+                        if (PAIR) acc_u[c + j] = fmaf(uu[j], sa * wsu, acc_u[c + j]);
                     }
                 }
                 tc_fence_before();
                 mbar_arrive(tempty_bar(a));
             }
             if (!ok) break;
+            if (S > 1) {
+                // this unit's fp32 partial, [col][128 rows]: a warp writes 128 contiguous bytes
+                float* pu = args.part + (size_t)u * C::kCols * 128 + et;
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    if (j < nl) {
+                        pu[(size_t)j * 128] = acc_g[j];
+                        if (PAIR) pu[(size_t)(NT + j) * 128] = acc_u[PAIR ? j : 0];
+                    }
+                }
+                __threadfence();
+                if (!epi_sync()) break;
+                if (et == 0) s_last = (atomicAdd(args.cnt + t, 1) == S - 1);
+                if (!epi_sync()) break;
+                if (!s_last) continue;
+                __threadfence();
+                // last unit of the tile: the S partials, summed in split order
+                const float* pt = args.part + (size_t)t * S * C::kCols * 128 + et;
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    if (j < nl) {
+                        float g = 0.0f, v2 = 0.0f;
+                        for (int s2 = 0; s2 < S; ++s2) {
+                            g += __ldcg(pt + ((size_t)s2 * C::kCols + j) * 128);
+                            if (PAIR) v2 += __ldcg(pt + ((size_t)s2 * C::kCols + NT + j) * 128);
+                        }
+                        acc_g[j] = g;
+                        if (PAIR) acc_u[PAIR ? j : 0] = v2;
+                    }
+                }
+                if (et == 0) args.cnt[t] = 0;
+            }
             // store: this thread owns output column n for the tile's rows
             const int n = nb * 128 + q * 32 + lane;
 #pragma unroll
@@ -387,8 +451,9 @@ constexpr int kSegThreads = 1024;
 
 __global__ void __launch_bounds__(kSegThreads, 1)
     derive_segments_kernel(const int32_t* __restrict__ m, int M, int E, int32_t* __restrict__ seg,
-                           DevCtl ctl) {
+                           DevCtl ctl, int* __restrict__ cnt = nullptr, int ncnt = 0) {
     extern __shared__ int sm[];
+    for (int i = threadIdx.x; i < ncnt; i += kSegThreads) cnt[i] = 0;   // split-K tile counters
     int* nst = sm;
     int* fst = sm + E;
     int* lst = sm + 2 * E;
@@ -431,13 +496,14 @@ __global__ void __launch_bounds__(kSegThreads, 1)
 template <int NT, bool PAIR>
 int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
-               int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
+               int K, int E, cudaStream_t stream, const OutMap& om = OutMap{},
+               const SplitWs& sw = SplitWs{}) {
     using C = Cfg<NT, PAIR>;
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
                           128, true);
     if (rc != FERRET_OK) return rc;
-    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, NT, true);
+    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, kABox, true);
     if (rc != FERRET_OK) return rc;
     const int nk = K / 128;
     const int budget = info->max_smem_optin - 1024;   // 1 KB for base alignment
@@ -466,6 +532,10 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     g.K = K;
     g.E = E;
     g.stages = stages;
+    g.splits_max = sw.part ? sw.smax : 1;
+    g.part = sw.part;
+    g.cnt = sw.cnt;
+    g.part_bytes = sw.bytes;
     g.ctl = make_ctl(info);
     kern<<<info->num_sms, kThreads, smem, stream>>>(tm_w, tm_a, g);
     return launch_status();
@@ -839,6 +909,10 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.K = K;
     g.E = E;
     g.stages = stages;
+    g.splits_max = 1;
+    g.part = nullptr;
+    g.cnt = nullptr;
+    g.part_bytes = 0;
     g.ctl = make_ctl(info);
     kern<<<info->num_sms, kPfThreads, smem, stream>>>(tm_w, tm_a, g);
     return launch_status();
@@ -876,7 +950,8 @@ bool use_prefill(int M, int E, int flags, int N) {
 
 int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                  const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M, int N,
-                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om) {
+                 int K, int E, int flags, int rows_hint, cudaStream_t s, const OutMap& om,
+                 const SplitWs& sw) {
     const bool pair = (flags & FERRET_SILU_MUL) != 0;
     if (use_prefill(rows_hint, E, flags, N))
         return pair ? launch_fp8_prefill<true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
@@ -886,16 +961,16 @@ int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, co
 #define FERRET_FP8_CASE(NT_)                                                                    \
     case NT_:                                                                                   \
         return pair ? launch_fp8<NT_, true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M, \
-                                            N, K, E, s, om)                                     \
+                                            N, K, E, s, om, sw)                                 \
                     : launch_fp8<NT_, false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,\
-                                             N, K, E, s, om);
+                                             N, K, E, s, om, sw);
     switch (pick_tile(rows_hint, E, flags, pair)) {
         FERRET_FP8_CASE(16)
         FERRET_FP8_CASE(32)
         FERRET_FP8_CASE(64)
         case 128:
             return launch_fp8<128, false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M, N,
-                                          K, E, s, om);
+                                          K, E, s, om, sw);
         default:
             return FERRET_ERR_SHAPE;
     }
@@ -906,9 +981,17 @@ int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, co
 
 using namespace ferret;
 
+// Batches up to kSplitMaxRows rows also get room for split-K partials (a
+// launch with fewer tiles than SMs splits K across them).
+constexpr int kSplitMaxRows = 4096;
+constexpr size_t kSplitBytes = (size_t)16 << 20;
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
 extern "C" size_t ferret_fp8_grouped_gemm_workspace_size(int M, int E) {
-    (void)M;
-    return E > 0 ? (size_t)E * 2 * sizeof(int32_t) : 0;
+    if (E <= 0) return 0;
+    const size_t seg = align256((size_t)E * 2 * sizeof(int32_t));
+    return M >= 0 && M <= kSplitMaxRows ? seg + kSplitBytes : seg;
 }
 
 extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
@@ -932,23 +1015,44 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
 
     const int32_t* seg = expert_offsets;
     int seg_pairs = 0;
+    const size_t seg_bytes = expert_offsets ? 0 : align256((size_t)E * 2 * sizeof(int32_t));
+    if (!expert_offsets && (!workspace || ws_bytes < seg_bytes)) return FERRET_ERR_WORKSPACE;
+    if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 3u)) return FERRET_ERR_ALIGN;
+    // split-K room past the segments: tile counters (bounded by the tiles any
+    // token tile of >= 16 rows can give), then fp32 partials
+    SplitWs sw;
+    int ncnt = 0;
+    if (workspace && M <= kSplitMaxRows && ws_bytes > seg_bytes) {
+        const long long tiles_up = ((long long)std::min(M, E) + M / 16) * (N / 128);
+        const size_t cnt_bytes = align256((size_t)tiles_up * sizeof(int));
+        if (ws_bytes > seg_bytes + cnt_bytes + 4096) {
+            uint8_t* base = static_cast<uint8_t*>(workspace) + seg_bytes;
+            sw.cnt = reinterpret_cast<int*>(base);
+            sw.part = reinterpret_cast<float*>(base + cnt_bytes);
+            sw.bytes = ws_bytes - seg_bytes - cnt_bytes;
+            sw.smax = K / 128;
+            ncnt = (int)tiles_up;
+        }
+    }
     if (!expert_offsets) {
-        if (!workspace || ws_bytes < ferret_fp8_grouped_gemm_workspace_size(M, E))
-            return FERRET_ERR_WORKSPACE;
-        if ((reinterpret_cast<uintptr_t>(workspace) & 3u)) return FERRET_ERR_ALIGN;
         const int smem = 3 * E * (int)sizeof(int);
         derive_segments_kernel<<<1, kSegThreads, smem, s>>>(m_indices, M, E,
                                                             static_cast<int32_t*>(workspace),
-                                                            make_ctl(info));
+                                                            make_ctl(info), sw.cnt, ncnt);
         if ((rc = launch_status()) != FERRET_OK) return rc;
         seg = static_cast<const int32_t*>(workspace);
         seg_pairs = 1;
+    } else if (sw.cnt) {
+        if (cudaMemsetAsync(sw.cnt, 0, (size_t)ncnt * sizeof(int), s) != cudaSuccess) {
+            cudaGetLastError();
+            return FERRET_ERR_CUDA;
+        }
     }
 
     // many tokens per expert: the prefill kernel (tokens on MMA M, 256 weight rows on N);
     // otherwise the swap-AB kernel with a token tile sized to the rows per expert
     return run_fp8_gemm(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, seg_pairs, M, N, K, E,
-                        flags, M, s, OutMap{});
+                        flags, M, s, OutMap{}, sw);
 }
 
 #include <mutex>

@@ -141,6 +141,11 @@ FERRET_API int ferret_fp8_gather_rows(const void* q_fp8, const float* q_scale, i
  *   m_indices (needs ferret_fp8_grouped_gemm_workspace_size() bytes of
  *   workspace); non-NULL int32 [E+1] -> rows [off[e], off[e+1]) belong to
  *   expert e (m_indices is then not read and may be NULL).
+ * workspace (4-byte aligned): with M <= 4096, ferret_fp8_grouped_gemm_workspace_size
+ *   also reserves room for split-K: a launch with fewer tiles than half the
+ *   SMs then splits K over them and reduces the fp32 partials in a fixed order
+ *   (deterministic).  A smaller workspace (or NULL with expert_offsets) only
+ *   disables the split.
  * Limits: K % 128 == 0, N % 128 == 0 (N % 256 == 0 with SILU), E <= 1024,
  *   K <= 16384; pointers 16-byte aligned.
  */

@@ -46,7 +46,9 @@ def test_version_and_strerror(L):
 
 
 def test_workspace_size(L):
-    assert L.ferret_fp8_grouped_gemm_workspace_size(1024, 256) == 256 * 2 * 4
+    # segments (2E ints, 256-byte padded); up to 4096 rows also 16 MB of split-K room
+    assert L.ferret_fp8_grouped_gemm_workspace_size(8192, 256) == 256 * 2 * 4
+    assert L.ferret_fp8_grouped_gemm_workspace_size(1024, 256) == 256 * 2 * 4 + (16 << 20)
     assert L.ferret_fp8_grouped_gemm_workspace_size(1, 0) == 0
 
 

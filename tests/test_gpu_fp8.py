@@ -235,6 +235,15 @@ CASES = [
     ([300, 129, 2, 0, 77], 512, 384, 0, True, 128),
     ([40, 40, 40, 40], 256, 128, 5, False, 128),
     ([1000], 256, 256, 0, True, 128),
+    # per-tile MMA N (16-row granules) inside a 64- or 128-row token tile
+    ([1, 17, 33, 49, 64, 0, 70], 256, 512, 0, False, 64),
+    ([1, 17, 33, 49, 64, 0, 70], 512, 512, 0, True, 64),
+    ([5, 100, 127, 128, 129], 256, 384, 0, False, 128),
+    # few tiles: K split over the SMs (m_indices path, with workspace), fp32
+    # partials reduced in split order by the last unit of each tile
+    ([32], 1024, 2048, 0, False, 0),
+    ([32], 1024, 2048, 0, True, 0),
+    ([3, 0, 9], 512, 7168, 0, True, 16),
 ]
 
 
