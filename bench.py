@@ -166,6 +166,23 @@ def roofline(byts, flops, kernel_ms, pk, kernel):
     return out
 
 
+def graph_of(fn):
+    """fn's launches captured once as a CUDA graph: timing its replays measures
+    device time without the Python/ctypes launch overhead, which would
+    otherwise dominate microsecond-sized steps."""
+    import torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    return g
+
+
 def read_traffic(kernel_tag):
     """dram bytes per launch recorded from an ncu capture in profiles/<tag>.md."""
     path = os.path.join(ROOT, "profiles", f"{kernel_tag}.md")
@@ -285,10 +302,12 @@ def run_single(args, cfg):
         torch.cuda.synchronize()
         return [a.elapsed_time(b) for a, b in evs]
 
+    # each timed step replays the step's launches as one CUDA graph
+    step_graph = graph_of(step)
     clocks = Clocks(torch.cuda.current_device())
     torch.cuda.synchronize()
     clocks.start()
-    step_ms = timed(step, args.steps)
+    step_ms = timed(step_graph.replay, args.steps)
     clk = clocks.stop()
     torch.cuda.synchronize()
 
@@ -296,7 +315,7 @@ def run_single(args, cfg):
     def gemm():
         ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
                                              expert_offsets=bufs.offsets, silu=cfg.silu)
-    gemm_ms = timed(gemm, args.steps)
+    gemm_ms = timed(graph_of(gemm).replay, args.steps)
 
     # end to end through the public API with host buffers
     h_hidden = hidden.cpu().pin_memory()
@@ -407,13 +426,15 @@ def run_single_int4(args, cfg):
         torch.cuda.synchronize()
         return [a.elapsed_time(b) for a, b in evs]
 
+    step_graph = graph_of(step)
     clocks = Clocks(torch.cuda.current_device())
     clocks.start()
-    step_ms = timed(step, args.steps)
+    step_ms = timed(step_graph.replay, args.steps)
     clk = clocks.stop()
     perm = ops.moe_permute(ids, cfg.E)
-    gemm_ms = timed(lambda: ops.moe_wna16_w13(hidden, packed, ids, silu=cfg.silu, out=out,
-                                              perm=perm, workspace=ws), args.steps)
+    gemm_ms = timed(graph_of(lambda: ops.moe_wna16_w13(hidden, packed, ids, silu=cfg.silu, out=out,
+                                                       perm=perm, workspace=ws)).replay,
+                    args.steps)
     h_hidden, h_ids = hidden.cpu().pin_memory(), ids.cpu().pin_memory()
     h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     d_hidden, d_ids = torch.empty_like(hidden), torch.empty_like(ids)
@@ -567,7 +588,8 @@ def run_v007_suite(args):
         mi_tile = mi[(torch.arange(M, device=dev) // 128) * 128].contiguous()
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         for m_ind, rd, ud in ((mi, res, us), (mi_tile, res_tile, us_tile)):
-            run = lambda: ops.m_grouped_fp8_gemm_nt_contiguous((A, As), (W, Ws), out, m_ind)
+            call = lambda: ops.m_grouped_fp8_gemm_nt_contiguous((A, As), (W, Ws), out, m_ind)
+            run = graph_of(call).replay
             for _ in range(20):
                 run()
             torch.cuda.synchronize()
@@ -588,7 +610,8 @@ def run_v007_suite(args):
         raise RuntimeError("device status error")
     return {"suite": "v007-configs", "impl": "ours", "unit": "TFLOPS", "results": res, "us": us,
             "results_tile_expert": res_tile, "us_tile_expert": us_tile,
-            "timing": "median of 100, 256 MB flush before each, CUDA events",
+            "timing": "median of 100, 256 MB flush before each, CUDA events around a CUDA-graph "
+                      "replay of the call",
             "numerics": "exact fp32 block scales, per-row experts; *_tile_expert: the same call "
                         "with m_indices set to each 128-row tile's first expert (the work the "
                         "reference kernel does)"}

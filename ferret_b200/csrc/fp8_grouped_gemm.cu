@@ -59,16 +59,20 @@ struct GemmArgs {
     int peer_rows;
     int M, N, K, E;
     int stages;
-    // split-K for launches with fewer tiles than SMs (swap-AB kernel): the
-    // kernel picks S <= splits_max from the actual tile count so that the
-    // fp32 partials part[unit][col][128] fit part_bytes; cnt[tile] (zeroed
-    // before the launch) finds the last unit of a tile, which reduces in
-    // split order.  splits_max <= 1 disables it.
+    DevCtl ctl;
+};
+
+// Split-K for launches with fewer tiles than SMs (swap-AB kernel): the kernel
+// picks S <= splits_max from the actual tile count so that the fp32 partials
+// part[unit][col][128] fit part_bytes; cnt[tile] (zeroed before the launch)
+// finds the last unit of a tile, which reduces in split order.  splits_max <= 1
+// disables it.  (A separate kernel argument: the prefill kernel's code
+// generation measured sensitive to the size of its argument struct.)
+struct SplitArgs {
     int splits_max;
     float* part;
     int* cnt;
     size_t part_bytes;
-    DevCtl ctl;
 };
 
 template <int NT, bool PAIR>
@@ -152,7 +156,8 @@ __device__ __forceinline__ void decode_tile(int t, int nbc, int E, const int* mt
 template <int NT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_w,
-                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
+                           const SplitArgs split) {
     using C = Cfg<NT, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
@@ -230,10 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tiles = mt_start[E] * nbc;
     // split-K when the tiles cannot fill the SMs (every CTA derives the same S)
     int S = 1;
-    if (args.splits_max > 1 && tiles > 0 && 2 * tiles <= (int)gridDim.x) {
-        S = min((int)gridDim.x / tiles, min(args.splits_max, nk));
+    if (split.splits_max > 1 && tiles > 0 && 2 * tiles <= (int)gridDim.x) {
+        S = min((int)gridDim.x / tiles, min(split.splits_max, nk));
         const size_t unit_bytes = (size_t)C::kCols * 128 * sizeof(float);
-        while (S > 1 && (size_t)tiles * S * unit_bytes > args.part_bytes) --S;
+        while (S > 1 && (size_t)tiles * S * unit_bytes > split.part_bytes) --S;
     }
     const int total = tiles * S;                  // work units: (tile, K split)
 
@@ -387,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             if (S > 1) {
                 // this unit's fp32 partial, [col][128 rows]: a warp writes 128 contiguous bytes
-                float* pu = args.part + (size_t)u * C::kCols * 128 + et;
+                float* pu = split.part + (size_t)u * C::kCols * 128 + et;
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
                     if (j < nl) {
@@ -397,12 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 __threadfence();
                 if (!epi_sync()) break;
-                if (et == 0) s_last = (atomicAdd(args.cnt + t, 1) == S - 1);
+                if (et == 0) s_last = (atomicAdd(split.cnt + t, 1) == S - 1);
                 if (!epi_sync()) break;
                 if (!s_last) continue;
                 __threadfence();
                 // last unit of the tile: the S partials, summed in split order
-                const float* pt = args.part + (size_t)t * S * C::kCols * 128 + et;
+                const float* pt = split.part + (size_t)t * S * C::kCols * 128 + et;
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
                     if (j < nl) {
@@ -415,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (PAIR) acc_u[PAIR ? j : 0] = v2;
                     }
                 }
-                if (et == 0) args.cnt[t] = 0;
+                if (et == 0) split.cnt[t] = 0;
             }
             // store: this thread owns output column n for the tile's rows
             const int n = nb * 128 + q * 32 + lane;
@@ -532,12 +537,13 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     g.K = K;
     g.E = E;
     g.stages = stages;
-    g.splits_max = sw.part ? sw.smax : 1;
-    g.part = sw.part;
-    g.cnt = sw.cnt;
-    g.part_bytes = sw.bytes;
     g.ctl = make_ctl(info);
-    kern<<<info->num_sms, kThreads, smem, stream>>>(tm_w, tm_a, g);
+    SplitArgs sp;
+    sp.splits_max = sw.part ? sw.smax : 1;
+    sp.part = sw.part;
+    sp.cnt = sw.cnt;
+    sp.part_bytes = sw.bytes;
+    kern<<<info->num_sms, kThreads, smem, stream>>>(tm_w, tm_a, g, sp);
     return launch_status();
 }
 
@@ -583,9 +589,13 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
     o += 4 * (E + 1);
     L.part_off = o;
     o += 4 * (kPfThreads + 1);
-    o = (o + 15) & ~15;
+    o = (o + 7) & ~7;
     L.stg_off = o;
-    if (staged) o += kPfStgWarp * (kPfEpi / 32);
+    if (staged) {
+        o = (o + 15) & ~15;
+        L.stg_off = o;
+        o += kPfStgWarp * (kPfEpi / 32);
+    }
     L.bar_off = o;
     o += 8 * (2 * kPfMaxStages + 2 * 2 + 2);
     L.misc_off = o;
@@ -594,10 +604,7 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
     return L;
 }
 
-// STAGED: output rows written through shared memory, 64 contiguous bytes of
-// 8 rows per store instruction -- used when rows go to other GPUs, where
-// 16-byte writes scattered over 32 rows make poor NVLink transactions.
-template <bool PAIR, bool STAGED>
+template <bool PAIR>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
@@ -607,7 +614,245 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7;
     const int nbc = N >> 8;                        // 256-row weight tiles
-    const PfLayout L = pf_layout(NS, E, STAGED);
+    const PfLayout L = pf_layout(NS, E, false);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
+    const uint32_t epi_bar = drain_bar + 8u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kPfEpi);
+        }
+        mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kPfEpi);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        seg_s[e] = s;
+        seg_c[e] = c;
+        mt_start[e] = (c + 127) >> 7;
+    }
+    if (seg_bad) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
+            const uint64_t pol_a = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
+                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = stage_base + s * kPfStage;
+                    mbar_expect_tx(full_bar(s), kPfStage);
+                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
+                }
+            }
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (elect_one()) {
+            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
+                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPfStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
+                                   idesc, ks > 0);
+                    tc_commit(empty_bar(s));
+                    tc_commit(tfull_bar(a));
+                }
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else {
+        // ================= epilogue: promotion + store =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        RingPos ra;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int e, row0, rows, nb;
+            decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const bool live = r < rows;
+            const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                       args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(ra.slot));
+            }
+            if (!ok) break;
+            int orow = row0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + row0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            if (live && orow >= 0) {
+                __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
+                if (PAIR) {
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 pk;
+                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                        }
+                        dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// The same kernel for output rows on other GPUs (expert parallelism): rows are
+// written through shared memory, 64 contiguous bytes of 8 rows per store
+// instruction, because 16-byte writes scattered over 32 rows make poor NVLink
+// transactions.  A separate function rather than a template switch of the one
+// above, so that the local kernel's code generation stays as measured.
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_peer_kernel(const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;                        // 256-row weight tiles
+    const PfLayout L = pf_layout(NS, E, true);
     int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
     int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
@@ -783,46 +1028,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 orow = __ldg(args.out_rows + row0 + r);
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
-            if (!STAGED) {
-                if (live && orow >= 0) {
-                    __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
-                    if (PAIR) {
-                        uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
-#pragma unroll
-                        for (int c = 0; c < 64; c += 8) {
-                            uint4 pk;
-                            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const __nv_bfloat162 b = __floats2bfloat162_rn(
-                                    silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
-                                    silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
-                                pw[j] = *reinterpret_cast<const uint32_t*>(&b);
-                            }
-                            dst[c >> 3] = pk;
-                        }
-                    } else {
-                        uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
-                        uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
-#pragma unroll
-                        for (int c = 0; c < 64; c += 8) {
-                            uint4 p0, p1;
-                            uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
-                            uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
-                                const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
-                                w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
-                                w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
-                            }
-                            d0[c >> 3] = p0;
-                            d1[c >> 3] = p1;
-                        }
-                    }
-                }
-                continue;
-            }
             // Staged: every store instruction writes 64 contiguous bytes of 8
             // rows instead of 16 bytes of 32 rows.
             rowp[lane] = (live && orow >= 0) ? out_row_ptr(args, orow, ldo) : nullptr;
@@ -889,7 +1094,7 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E, STAGED).total) / kPfStage);
     if (stages < 2) return FERRET_ERR_SHAPE;
     const int smem = pf_layout(stages, E, STAGED).total + 1024;
-    auto kern = fp8_w13_prefill_kernel<PAIR, STAGED>;
+    auto kern = STAGED ? fp8_w13_prefill_peer_kernel<PAIR> : fp8_w13_prefill_kernel<PAIR>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
         cudaGetLastError();
         return FERRET_ERR_CUDA;
@@ -909,10 +1114,6 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.K = K;
     g.E = E;
     g.stages = stages;
-    g.splits_max = 1;
-    g.part = nullptr;
-    g.cnt = nullptr;
-    g.part_bytes = 0;
     g.ctl = make_ctl(info);
     kern<<<info->num_sms, kPfThreads, smem, stream>>>(tm_w, tm_a, g);
     return launch_status();
@@ -928,11 +1129,14 @@ int launch_fp8_prefill(const DeviceInfo* info, const void* a, const float* a_sca
                                                         seg_pairs, M, N, K, E, stream, om);
 }
 
-int pick_tile(int M, int E, int flags, bool pair) {
+int pick_tile(int M, int E, int K, int flags, bool pair) {
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
     if (nt == 0) {
+        // measured on B200 (graph-timed): at K = 7168 the 32-row tile streams
+        // the decode weights 4 % faster than the 16-row one (same tiles, one
+        // stage fewer); at K = 2048 the 16-row tile is faster
         const int avg = (M + E - 1) / std::max(E, 1);
-        nt = avg <= 12 ? 16 : avg <= 24 ? 32 : avg <= 48 ? 64 : 128;
+        nt = (avg <= 12 && K < 4096) ? 16 : avg <= 24 ? 32 : avg <= 48 ? 64 : 128;
     }
     if (pair && nt > 64) nt = 64;
     return nt;
@@ -964,7 +1168,7 @@ int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, co
                                             N, K, E, s, om, sw)                                 \
                     : launch_fp8<NT_, false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,\
                                              N, K, E, s, om, sw);
-    switch (pick_tile(rows_hint, E, flags, pair)) {
+    switch (pick_tile(rows_hint, E, K, flags, pair)) {
         FERRET_FP8_CASE(16)
         FERRET_FP8_CASE(32)
         FERRET_FP8_CASE(64)
@@ -1122,7 +1326,7 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
     derive_segments_kernel<<<1, kSegThreads, 3 * E * (int)sizeof(int), s>>>(m_indices, M, E, seg,
                                                                            make_ctl(info));
     if ((rc = launch_status()) != FERRET_OK) return rc;
-    const int nt = pick_tile(M, E, flags, pair);
+    const int nt = pick_tile(M, E, K, flags, pair);
     switch (nt) {
         case 16:
             return pair ? launch_fp8<16, true>(info, a_fp8, a_scale, w_fp8, w_scale, out_bf16, seg, 1, M, N, K, E, s)
