@@ -173,6 +173,7 @@ namespace ferret {
 namespace {
 
 __global__ void wait_timeout_selftest_kernel(DevCtl ctl) {
+    pdl_begin();
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
@@ -195,6 +196,5 @@ extern "C" int ferret_selftest_wait_timeout(unsigned long long timeout_ns, void*
     if (rc != FERRET_OK) return rc;
     DevCtl c = make_ctl(info);
     c.timeout_ns = timeout_ns;
-    wait_timeout_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>(c);
-    return launch_status();
+    return launch_kernel(wait_timeout_selftest_kernel, dim3(1), dim3(32), 0, as_stream(stream), c);
 }

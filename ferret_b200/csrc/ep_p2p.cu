@@ -106,6 +106,7 @@ __device__ bool ep_barrier(const EpDev& d, int slot_base, uint32_t epoch, DevCtl
 // zeroed here (no rank's GEMM writes them).  Grid-wide, one id per thread.
 __global__ void __launch_bounds__(kGatherThreads)
     ep_publish_kernel(const EpDev d, const int32_t* __restrict__ topk_ids) {
+    pdl_begin();
     const int own = d.T * d.topk;
     for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < own; i += gridDim.x * kGatherThreads) {
         const int id = topk_ids[i];
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(kGatherThreads)
 // system fence: the quantized rows, ids and zeroed rows written by the
 // kernels before this one are visible first), wait for every rank's.
 __global__ void __launch_bounds__(32, 1) ep_ready_kernel(const EpDev d, DevCtl ctl) {
+    pdl_begin();
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) {
         s_epoch = *d.epoch + 1u;
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(32, 1) ep_ready_kernel(const EpDev d, DevCtl c
 // is empty and touches no peer memory.
 __global__ void __launch_bounds__(kGatherThreads)
     ep_ids_kernel(const EpDev d) {
+    pdl_begin();
     const int own = d.T * d.topk;
     const int total = d.world * own;
     const bool failed = *d.failed != 0;
@@ -156,6 +159,7 @@ __global__ void __launch_bounds__(kGatherThreads)
 // the NVLink latency is paid once per row, not once per load.
 __global__ void __launch_bounds__(kGatherThreads)
     ep_gather_kernel(const EpDev d) {
+    pdl_begin();
     constexpr int kMaxVec = 16;
     const int rows = d.offsets[d.El];
     const int lane = threadIdx.x & 31;
@@ -198,6 +202,7 @@ __global__ void __launch_bounds__(kGatherThreads)
 }
 
 __global__ void __launch_bounds__(32, 1) ep_done_kernel(const EpDev d, DevCtl ctl) {
+    pdl_begin();
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) {
         __threadfence_system();     // this rank's peer stores (the GEMM) before the flag
@@ -472,16 +477,14 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     {
         const int want = (own + kGatherThreads - 1) / kGatherThreads;
         const int grid = want < info->num_sms * 4 ? want : info->num_sms * 4;
-        ep_publish_kernel<<<grid, kGatherThreads, 0, s>>>(d, topk_ids);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(ep_publish_kernel, dim3(grid), dim3(kGatherThreads), 0, s, d,
+                                topk_ids)) != FERRET_OK) return rc;
     }
-    ep_ready_kernel<<<1, 32, 0, s>>>(d, ctl);
-    if ((rc = launch_status()) != FERRET_OK) return rc;
+    if ((rc = launch_kernel(ep_ready_kernel, dim3(1), dim3(32), 0, s, d, ctl)) != FERRET_OK) return rc;
     {
         const int want = (pairs + kGatherThreads - 1) / kGatherThreads;
         const int grid = want < info->num_sms * 4 ? want : info->num_sms * 4;
-        ep_ids_kernel<<<grid, kGatherThreads, 0, s>>>(d);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(ep_ids_kernel, dim3(grid), dim3(kGatherThreads), 0, s, d)) != FERRET_OK) return rc;
     }
     // 3. local expert order of all pairs
     rc = ferret_moe_permute(c->all_ids, c->world * T, c->topk, c->El, c->sorted, c->offsets,
@@ -491,8 +494,7 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     {
         const int want = (pairs + kGatherThreads / 32 - 1) / (kGatherThreads / 32);
         const int grid = want < info->num_sms * 8 ? want : info->num_sms * 8;
-        ep_gather_kernel<<<grid, kGatherThreads, 0, s>>>(d);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(ep_gather_kernel, dim3(grid), dim3(kGatherThreads), 0, s, d)) != FERRET_OK) return rc;
     }
     // 5. grouped GEMM, epilogue stores into the source ranks' output buffers
     OutMap om;
@@ -504,8 +506,7 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
                       c->N, c->K, c->El, c->flags, own, s, om);
     if (rc != FERRET_OK) return rc;
     // 6. every rank's rows have landed
-    ep_done_kernel<<<1, 32, 0, s>>>(d, ctl);
-    if ((rc = launch_status()) != FERRET_OK) return rc;
+    if ((rc = launch_kernel(ep_done_kernel, dim3(1), dim3(32), 0, s, d, ctl)) != FERRET_OK) return rc;
     // 7. to the caller's buffer
     if (out_bf16 && out_bf16 != my + c->off_out) {
         if (cudaMemcpyAsync(out_bf16, my + c->off_out, (size_t)own * c->n_out * 2,

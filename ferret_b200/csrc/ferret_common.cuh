@@ -347,6 +347,17 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Programmatic dependent launch: every kernel of the library is launched
+// with programmatic stream serialization, so the next kernel in the stream
+// can be scheduled while this one runs.  Each kernel therefore first waits
+// until the previous grid in the stream has completed and its memory is
+// visible (griddepcontrol.wait; a no-op without a programmatic predecessor),
+// then lets its own dependent launch early.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

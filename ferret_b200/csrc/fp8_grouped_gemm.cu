@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fp8_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
                            const SplitArgs split) {
+    pdl_begin();
     using C = Cfg<NT, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
@@ -456,7 +457,8 @@ constexpr int kSegThreads = 1024;
 
 __global__ void __launch_bounds__(kSegThreads, 1)
     derive_segments_kernel(const int32_t* __restrict__ m, int M, int E, int32_t* __restrict__ seg,
-                           DevCtl ctl, int* __restrict__ cnt = nullptr, int ncnt = 0) {
+                           DevCtl ctl, int* __restrict__ cnt, int ncnt) {
+    pdl_begin();
     extern __shared__ int sm[];
     for (int i = threadIdx.x; i < ncnt; i += kSegThreads) cnt[i] = 0;   // split-K tile counters
     int* nst = sm;
@@ -543,8 +545,7 @@ int launch_fp8(const DeviceInfo* info, const void* a, const float* a_scale, cons
     sp.part = sw.part;
     sp.cnt = sw.cnt;
     sp.part_bytes = sw.bytes;
-    kern<<<info->num_sms, kThreads, smem, stream>>>(tm_w, tm_a, g, sp);
-    return launch_status();
+    return launch_kernel(kern, dim3(info->num_sms), dim3(kThreads), smem, stream, tm_w, tm_a, g, sp);
 }
 
 // ---------------------------------------------------------------------------
@@ -608,6 +609,7 @@ template <bool PAIR>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -846,6 +848,7 @@ template <bool PAIR>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_peer_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1115,8 +1118,7 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.E = E;
     g.stages = stages;
     g.ctl = make_ctl(info);
-    kern<<<info->num_sms, kPfThreads, smem, stream>>>(tm_w, tm_a, g);
-    return launch_status();
+    return launch_kernel(kern, dim3(info->num_sms), dim3(kPfThreads), smem, stream, tm_w, tm_a, g);
 }
 
 template <bool PAIR>
@@ -1240,10 +1242,9 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous(
     }
     if (!expert_offsets) {
         const int smem = 3 * E * (int)sizeof(int);
-        derive_segments_kernel<<<1, kSegThreads, smem, s>>>(m_indices, M, E,
-                                                            static_cast<int32_t*>(workspace),
-                                                            make_ctl(info), sw.cnt, ncnt);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(derive_segments_kernel, dim3(1), dim3(kSegThreads), smem, s,
+                                m_indices, M, E, static_cast<int32_t*>(workspace), make_ctl(info),
+                                sw.cnt, ncnt)) != FERRET_OK) return rc;
         seg = static_cast<const int32_t*>(workspace);
         seg_pairs = 1;
     } else if (sw.cnt) {
@@ -1323,9 +1324,9 @@ extern "C" int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
     int32_t* seg = g_noalloc_ptr[info->device];
     cudaStream_t s = as_stream(stream);
     // every call rewrites all 2E (start, count) entries before the GEMM reads them
-    derive_segments_kernel<<<1, kSegThreads, 3 * E * (int)sizeof(int), s>>>(m_indices, M, E, seg,
-                                                                           make_ctl(info));
-    if ((rc = launch_status()) != FERRET_OK) return rc;
+    if ((rc = launch_kernel(derive_segments_kernel, dim3(1), dim3(kSegThreads),
+                            3 * E * (int)sizeof(int), s, m_indices, M, E, seg, make_ctl(info),
+                            (int*)nullptr, 0)) != FERRET_OK) return rc;
     const int nt = pick_tile(M, E, K, flags, pair);
     switch (nt) {
         case 16:

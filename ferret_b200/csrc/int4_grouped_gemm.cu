@@ -156,6 +156,7 @@ __device__ __forceinline__ void i4_decode_tile(int t, int nbc, int E, const int*
 template <int NT, bool PAIR>
 __global__ void __launch_bounds__(kI4Threads, 1)
     int4_w13_grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const Int4Args args) {
+    pdl_begin();
     using C = I4Cfg<NT, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
@@ -491,6 +492,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
 // {0,2,4,6,1,3,5,7}, then 4 x 128 bf16 scales [g][n].
 __global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint16_t* __restrict__ sc,
                                    uint32_t* __restrict__ blob, int E, int K, int N) {
+    pdl_begin();
     const int nbn = N >> 7, nbk = K >> 7;
     const size_t words_per_block = kBlob / 4;                 // 2304
     const size_t total = (size_t)E * nbn * nbk * words_per_block;
@@ -526,6 +528,7 @@ __global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint1
 __global__ void gather_rows_kernel(const uint4* __restrict__ hidden, const int32_t* __restrict__ rows,
                                    int topk, int T, int R, int K, uint4* __restrict__ out,
                                    int* __restrict__ cnt, int ncnt, DevCtl ctl) {
+    pdl_begin();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x)
         cnt[i] = 0;
     const int per_row = K >> 3;                                // 16-byte chunks
@@ -602,8 +605,7 @@ int launch_int4(const DeviceInfo* info, const void* a_sorted, const uint8_t* blo
             a.part = reinterpret_cast<float*>(split_ws + ((cnt_bytes + 255) & ~size_t(255)));
         }
     }
-    kern<<<info->num_sms, kI4Threads, smem, stream>>>(tm_a, a);
-    return launch_status();
+    return launch_kernel(kern, dim3(info->num_sms), dim3(kI4Threads), smem, stream, tm_a, a);
 }
 
 }  // namespace
@@ -639,10 +641,10 @@ extern "C" int ferret_int4_repack_w13(const int32_t* w_raw, const void* w_scale_
     if (rc != FERRET_OK) return rc;
     const size_t words = ferret_int4_blob_bytes(E, K, N) / 4;
     const int grid = (int)std::min<size_t>((words + 255) / 256, (size_t)info->num_sms * 16);
-    int4_repack_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint32_t*>(w_raw), static_cast<const uint16_t*>(w_scale_bf16),
-        static_cast<uint32_t*>(w_blob), E, K, N);
-    return launch_status();
+    return launch_kernel(int4_repack_kernel, dim3(grid), dim3(256), 0, as_stream(stream),
+                         reinterpret_cast<const uint32_t*>(w_raw),
+                         static_cast<const uint16_t*>(w_scale_bf16),
+                         static_cast<uint32_t*>(w_blob), E, K, N);
 }
 
 extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
@@ -687,11 +689,10 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
     {
         const size_t chunks = (size_t)R * (K / 8);
         const int grid = (int)std::min<size_t>((chunks + 255) / 256, (size_t)info->num_sms * 8);
-        gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(hidden_bf16), sorted_rows,
-                                                topk, T, R, K, static_cast<uint4*>(workspace),
-                                                reinterpret_cast<int*>(split_ws), ncnt,
-                                                make_ctl(info));
-        if ((rc = launch_status()) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(gather_rows_kernel, dim3(grid), dim3(256), 0, s,
+                                static_cast<const uint4*>(hidden_bf16), sorted_rows, topk, T, R, K,
+                                static_cast<uint4*>(workspace), reinterpret_cast<int*>(split_ws),
+                                ncnt, make_ctl(info))) != FERRET_OK) return rc;
     }
 #define FERRET_I4_CASE(NT_)                                                                        \
     case NT_:                                                                                      \

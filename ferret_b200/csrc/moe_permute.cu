@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     moe_permute_kernel(const int32_t* __restrict__ ids, int R, int E,
                        int32_t* __restrict__ sorted_rows, int32_t* __restrict__ offsets_out,
                        int32_t* __restrict__ m_indices) {
+    pdl_begin();
     extern __shared__ int smem[];
     int* hist = smem;                                   // [kPermWarps][E]
     int* offs = hist + kPermWarps * E;                  // [E+1]
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
 __global__ void __launch_bounds__(kPermThreads, 1)
     permute_count_kernel(const int32_t* __restrict__ ids, int R, int E, int chunk,
                          int32_t* __restrict__ counts) {
+    pdl_begin();
     extern __shared__ int hist[];                       // [kPermWarps][E]
     const int c0 = blockIdx.x * chunk, c1 = min(R, c0 + chunk);
     int lo, hi;
@@ -135,6 +137,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
 // expert e, in place; expert offsets.
 __global__ void __launch_bounds__(kScanThreads, 1)
     permute_scan_kernel(int32_t* __restrict__ counts, int C, int E, int32_t* __restrict__ offsets_out) {
+    pdl_begin();
     extern __shared__ int s[];
     int* tot = s;                   // [E+1]
     int* part = tot + E + 1;        // [kScanThreads+1]
@@ -161,6 +164,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     permute_scatter_kernel(const int32_t* __restrict__ ids, int R, int E, int chunk,
                            const int32_t* __restrict__ bases, const int32_t* __restrict__ offsets,
                            int32_t* __restrict__ sorted_rows, int32_t* __restrict__ m_indices) {
+    pdl_begin();
     extern __shared__ int hist[];                       // [kPermWarps][E]
     const int c0 = blockIdx.x * chunk, c1 = min(R, c0 + chunk);
     int lo, hi;
@@ -223,13 +227,12 @@ extern "C" int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int 
             cudaGetLastError();
             return FERRET_ERR_CUDA;
         }
-        permute_count_kernel<<<C, kPermThreads, hsm, s>>>(topk_ids, (int)R, E, chunk, counts);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
-        permute_scan_kernel<<<1, kScanThreads, ssm, s>>>(counts, C, E, expert_offsets);
-        if ((rc = launch_status()) != FERRET_OK) return rc;
-        permute_scatter_kernel<<<C, kPermThreads, hsm, s>>>(topk_ids, (int)R, E, chunk, counts,
-                                                           expert_offsets, sorted_rows, m_indices);
-        return launch_status();
+        if ((rc = launch_kernel(permute_count_kernel, dim3(C), dim3(kPermThreads), hsm, s,
+                                topk_ids, (int)R, E, chunk, counts)) != FERRET_OK) return rc;
+        if ((rc = launch_kernel(permute_scan_kernel, dim3(1), dim3(kScanThreads), ssm, s, counts,
+                                C, E, expert_offsets)) != FERRET_OK) return rc;
+        return launch_kernel(permute_scatter_kernel, dim3(C), dim3(kPermThreads), hsm, s, topk_ids,
+                             (int)R, E, chunk, counts, expert_offsets, sorted_rows, m_indices);
     }
     // one CTA over all ids (decode sizes, or no workspace given)
     const size_t smem = sizeof(int) * ((size_t)kPermWarps * E + E + 1 + kPermThreads + 1);
@@ -239,7 +242,6 @@ extern "C" int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int 
         cudaGetLastError();
         return FERRET_ERR_CUDA;
     }
-    moe_permute_kernel<<<1, kPermThreads, smem, s>>>(topk_ids, (int)R, E, sorted_rows,
-                                                     expert_offsets, m_indices);
-    return launch_status();
+    return launch_kernel(moe_permute_kernel, dim3(1), dim3(kPermThreads), smem, s, topk_ids,
+                         (int)R, E, sorted_rows, expert_offsets, m_indices);
 }

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     quant_act_kernel(const __nv_bfloat16* __restrict__ x, int x_rows,
                      const int32_t* __restrict__ gather, int gather_div, int R, int K,
                      uint8_t* __restrict__ q, float* __restrict__ scale, DevCtl ctl) {
+    pdl_begin();
     const int nk = K >> 7;
     const int tasks_per_row = (nk + kBlocksPerTask - 1) / kBlocksPerTask;
     const long long tasks = (long long)R * tasks_per_row;
@@ -120,10 +121,9 @@ extern "C" int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows,
     const long long tasks = (long long)R * ((K / 128 + kBlocksPerTask - 1) / kBlocksPerTask);
     const long long want = (tasks + (kQuantThreads / 32) - 1) / (kQuantThreads / 32);
     const int grid = (int)(want < (long long)info->num_sms * 16 ? want : (long long)info->num_sms * 16);
-    quant_act_kernel<<<grid, kQuantThreads, 0, as_stream(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x_bf16), x_rows, gather_rows, gather_div, R, K,
-        static_cast<uint8_t*>(a_fp8), a_scale, make_ctl(info));
-    return launch_status();
+    return launch_kernel(quant_act_kernel, dim3(grid), dim3(kQuantThreads), 0, as_stream(stream),
+                         static_cast<const __nv_bfloat16*>(x_bf16), x_rows, gather_rows,
+                         gather_div, R, K, static_cast<uint8_t*>(a_fp8), a_scale, make_ctl(info));
 }
 
 // ---------------------------------------------------------------------------
@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kGatherThreads)
     fp8_gather_rows_kernel(const uint4* __restrict__ q, const float* __restrict__ s, int src_rows,
                            const int32_t* __restrict__ rows, int div, int R, int K,
                            uint4* __restrict__ q_out, float* __restrict__ s_out, DevCtl ctl) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int vec = K >> 4, nk = K >> 7;
     const int warps = gridDim.x * (kGatherThreads / 32);
@@ -182,8 +183,7 @@ extern "C" int ferret_fp8_gather_rows(const void* q_fp8, const float* q_scale, i
     if (rc != FERRET_OK) return rc;
     const long long want = ((long long)R + kGatherThreads / 32 - 1) / (kGatherThreads / 32);
     const int grid = (int)(want < (long long)info->num_sms * 8 ? want : (long long)info->num_sms * 8);
-    fp8_gather_rows_kernel<<<grid, kGatherThreads, 0, as_stream(stream)>>>(
-        static_cast<const uint4*>(q_fp8), q_scale, src_rows, rows, div, R, K,
-        static_cast<uint4*>(out_fp8), out_scale, make_ctl(info));
-    return launch_status();
+    return launch_kernel(fp8_gather_rows_kernel, dim3(grid), dim3(kGatherThreads), 0,
+                         as_stream(stream), static_cast<const uint4*>(q_fp8), q_scale, src_rows,
+                         rows, div, R, K, static_cast<uint4*>(out_fp8), out_scale, make_ctl(info));
 }
