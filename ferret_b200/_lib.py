@@ -31,6 +31,9 @@ SIGNATURES = {
     "ferret_selftest_wait_timeout": (_i, [ctypes.c_ulonglong, _p]),
     "ferret_moe_permute": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "ferret_moe_permute_workspace_size": (_sz, [_i, _i, _i]),
+    "ferret_moe_align_block_size_sizes": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "ferret_moe_align_block_size_workspace_size": (_sz, [_i, _i, _i]),
+    "ferret_moe_align_block_size": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "ferret_quant_act_fp8_1x128": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_gather_rows": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous": (

@@ -17,6 +17,8 @@
 // chunks, one CTA each: a histogram kernel, a one-CTA scan kernel turning the
 // per-chunk counts into per-chunk bases, and a scatter kernel.
 // Integer-only; bit-exact with the CPU restatement.
+#include <algorithm>
+
 #include "capi_internal.h"
 
 namespace ferret {
@@ -244,4 +246,132 @@ extern "C" int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int 
     }
     return launch_kernel(moe_permute_kernel, dim3(1), dim3(kPermThreads), smem, s, topk_ids,
                          (int)R, E, sorted_rows, expert_offsets, m_indices);
+}
+
+// ---------------------------------------------------------------------------
+// Block-padded layout of vLLM's moe_align_block_size(topk_ids, block_size, E,
+// ignore_invalid_experts=True) (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126):
+// every expert's rows padded to a multiple of block_size, padding entries =
+// T*topk, expert_ids per block (-1 past the used blocks), and the padded total.
+// Built from the stable permutation above: one CTA turns the expert offsets
+// into padded offsets and block experts, then a grid fills the padded rows.
+// ---------------------------------------------------------------------------
+namespace ferret {
+namespace {
+
+constexpr int kPadThreads = 1024;
+
+__global__ void __launch_bounds__(kPadThreads, 1)
+    align_blocks_kernel(const int32_t* __restrict__ offs, int E, int bs, int max_blocks,
+                        int32_t* __restrict__ pad_offs, int32_t* __restrict__ expert_ids,
+                        int32_t* __restrict__ num_post_pad) {
+    pdl_begin();
+    extern __shared__ int sm[];
+    int* po = sm;                    // [E+1]
+    int* part = sm + E + 1;          // [kPadThreads+1]
+    for (int e = threadIdx.x; e < E; e += kPadThreads) {
+        const int c = offs[e + 1] - offs[e];
+        po[e] = (c + bs - 1) / bs * bs;
+    }
+    __syncthreads();
+    block_exclusive_scan(po, E, part);
+    for (int e = threadIdx.x; e <= E; e += kPadThreads) pad_offs[e] = po[e];
+    if (threadIdx.x == 0) *num_post_pad = po[E];
+    for (int b = threadIdx.x; b < max_blocks; b += kPadThreads) {
+        const int p = b * bs;
+        int v = -1;
+        if (p < po[E]) {
+            int lo = 0, hi = E - 1;          // last expert whose padded range starts at or before p
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (po[mid] <= p) lo = mid;
+                else hi = mid - 1;
+            }
+            v = lo;
+        }
+        expert_ids[b] = v;
+    }
+}
+
+__global__ void __launch_bounds__(256)
+    align_fill_kernel(const int32_t* __restrict__ sorted_rows, const int32_t* __restrict__ offs,
+                      const int32_t* __restrict__ pad_offs, int E, int max_padded, int sentinel,
+                      int32_t* __restrict__ sorted_ids) {
+    pdl_begin();
+    const int total = pad_offs[E];
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < max_padded; p += gridDim.x * blockDim.x) {
+        int v = sentinel;
+        if (p < total) {
+            int lo = 0, hi = E - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (pad_offs[mid] <= p) lo = mid;
+                else hi = mid - 1;
+            }
+            const int i = p - pad_offs[lo];
+            if (i < offs[lo + 1] - offs[lo]) v = sorted_rows[offs[lo] + i];
+        }
+        sorted_ids[p] = v;
+    }
+}
+
+}  // namespace
+}  // namespace ferret
+
+extern "C" int ferret_moe_align_block_size_sizes(int T, int topk, int E, int block_size,
+                                                  int* max_padded, int* max_blocks) {
+    if (T < 0 || topk <= 0 || E <= 0 || block_size <= 0 || !max_padded || !max_blocks)
+        return FERRET_ERR_SHAPE;
+    const long long numel = (long long)T * topk;
+    long long m = numel + (long long)E * (block_size - 1);
+    if (numel < E) m = std::min(m, numel * block_size);
+    if (m >= (1ll << 31)) return FERRET_ERR_SHAPE;
+    *max_padded = (int)m;
+    *max_blocks = (int)((m + block_size - 1) / block_size);
+    return FERRET_OK;
+}
+
+extern "C" size_t ferret_moe_align_block_size_workspace_size(int T, int topk, int E) {
+    if (T < 0 || topk <= 0 || E <= 0) return 0;
+    const size_t R = (size_t)T * topk;
+    const size_t perm = ferret_moe_permute_workspace_size(T, topk, E);
+    return (2 * R + 2 * ((size_t)E + 1)) * sizeof(int32_t) + 256 + perm;
+}
+
+extern "C" int ferret_moe_align_block_size(const int32_t* topk_ids, int T, int topk, int E,
+                                           int block_size, int32_t* sorted_ids,
+                                           int32_t* expert_ids, int32_t* num_tokens_post_pad,
+                                           void* workspace, size_t ws_bytes, void* stream) {
+    int max_padded = 0, max_blocks = 0;
+    int rc = ferret_moe_align_block_size_sizes(T, topk, E, block_size, &max_padded, &max_blocks);
+    if (rc != FERRET_OK) return rc;
+    if (E > 1024) return FERRET_ERR_SHAPE;
+    if (!sorted_ids || !expert_ids || !num_tokens_post_pad) return FERRET_ERR_NULL;
+    if (T > 0 && !topk_ids) return FERRET_ERR_NULL;
+    if (!workspace || ws_bytes < ferret_moe_align_block_size_workspace_size(T, topk, E))
+        return FERRET_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 3u) return FERRET_ERR_ALIGN;
+    DeviceInfo* info = nullptr;
+    if ((rc = current_device(&info)) != FERRET_OK) return rc;
+    cudaStream_t s = as_stream(stream);
+    const size_t R = (size_t)T * topk;
+    int32_t* w = static_cast<int32_t*>(workspace);
+    int32_t* rows = w;
+    int32_t* midx = rows + R;
+    int32_t* offs = midx + R;
+    int32_t* pad_offs = offs + E + 1;
+    uint8_t* pws = reinterpret_cast<uint8_t*>(pad_offs + E + 1);
+    pws += (256 - (reinterpret_cast<uintptr_t>(pws) & 255)) & 255;
+    const size_t pws_bytes = ferret_moe_permute_workspace_size(T, topk, E);
+    rc = ferret_moe_permute(topk_ids, T, topk, E, rows, offs, midx, pws_bytes ? pws : nullptr,
+                            pws_bytes, stream);
+    if (rc != FERRET_OK) return rc;
+    const size_t smem = sizeof(int) * ((size_t)E + 1 + kPadThreads + 1);
+    if ((rc = launch_kernel(align_blocks_kernel, dim3(1), dim3(kPadThreads), smem, s, offs, E,
+                            block_size, max_blocks, pad_offs, expert_ids, num_tokens_post_pad)) !=
+        FERRET_OK)
+        return rc;
+    const int grid = std::max(1, std::min((max_padded + 255) / 256, info->num_sms * 8));
+    return launch_kernel(align_fill_kernel, dim3(grid), dim3(256), 0, s, rows, offs, pad_offs, E,
+                         max_padded, (int)R, sorted_ids);
 }

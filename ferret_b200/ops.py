@@ -71,6 +71,33 @@ def moe_permute(topk_ids: torch.Tensor, num_experts: int):
     return sorted_rows, offsets, m_indices
 
 
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
+                         expert_map: torch.Tensor | None = None, pad_sorted_ids: bool = False,
+                         ignore_invalid_experts: bool = True):
+    """vLLM's moe_align_block_size (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126):
+    returns (sorted_token_ids, expert_ids, num_tokens_post_padded).  Ids outside
+    [0, E) are dropped (ignore_invalid_experts=True semantics); expert_map and
+    pad_sorted_ids are not supported."""
+    if expert_map is not None or pad_sorted_ids:
+        raise NotImplementedError("expert_map / pad_sorted_ids are not supported")
+    _need(topk_ids, torch.int32, "topk_ids", 2)
+    T, topk = topk_ids.shape
+    L = lib()
+    mp, mb = ctypes.c_int(0), ctypes.c_int(0)
+    check(L.ferret_moe_align_block_size_sizes(T, topk, num_experts, block_size, ctypes.byref(mp),
+                                              ctypes.byref(mb)), "ferret_moe_align_block_size_sizes")
+    dev = topk_ids.device
+    sorted_ids = torch.empty(mp.value, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty(mb.value, dtype=torch.int32, device=dev)
+    post = torch.empty(1, dtype=torch.int32, device=dev)
+    ws_bytes = int(L.ferret_moe_align_block_size_workspace_size(T, topk, num_experts))
+    ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.int32, device=dev)
+    check(L.ferret_moe_align_block_size(_ptr(topk_ids), T, topk, num_experts, block_size,
+                                        _ptr(sorted_ids), _ptr(expert_ids), _ptr(post), _ptr(ws),
+                                        ws_bytes, _stream()), "ferret_moe_align_block_size")
+    return sorted_ids, expert_ids, post
+
+
 def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = None,
                           gather_div: int = 1, out=None):
     """bf16 [rows, K] -> (e4m3 [R, K], f32 scales [R, K/128]).  With gather_rows,

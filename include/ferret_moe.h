@@ -95,6 +95,31 @@ FERRET_API int ferret_moe_permute(const int32_t* topk_ids, int T, int topk, int 
                        size_t ws_bytes, void* stream);
 
 /*
+ * Block-padded routing layout, the output of vLLM's
+ *   moe_align_block_size(topk_ids, block_size, E, ignore_invalid_experts=True)
+ *   (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126), built from the
+ *   stable permutation above.
+ * ferret_moe_align_block_size_sizes: max_padded = T*topk + E*(block_size-1)
+ *   (at most T*topk*block_size when T*topk < E), max_blocks =
+ *   ceil(max_padded / block_size) -- vLLM's buffer sizes.
+ * sorted_ids [max_padded]: every expert's flat (token, slot) indices in
+ *   ascending order, padded to a multiple of block_size with T*topk (also
+ *   past the used length); expert_ids [max_blocks]: the expert of each block,
+ *   -1 past the used blocks; num_tokens_post_pad [1]: the padded length.
+ * Ids outside [0, E) are dropped.  Order inside an expert is the ascending
+ * flat index (vLLM's own order inside an expert is not specified).
+ * workspace: ferret_moe_align_block_size_workspace_size(T, topk, E) bytes,
+ * 4-byte aligned.  Limits: E <= 1024.
+ */
+FERRET_API int ferret_moe_align_block_size_sizes(int T, int topk, int E, int block_size,
+                                                  int* max_padded, int* max_blocks);
+FERRET_API size_t ferret_moe_align_block_size_workspace_size(int T, int topk, int E);
+FERRET_API int ferret_moe_align_block_size(const int32_t* topk_ids, int T, int topk, int E,
+                                           int block_size, int32_t* sorted_ids,
+                                           int32_t* expert_ids, int32_t* num_tokens_post_pad,
+                                           void* workspace, size_t ws_bytes, void* stream);
+
+/*
  * Per-token 1x128 FP8 activation quantization (with optional row gather).
  * Replaces: DeepGEMM per_token_cast_to_fp8(x, use_ue8m0=False)
  *   (baselines/fp8-group-gemm/baseline_dsv3_decode.py:42).

@@ -133,6 +133,30 @@ def moe_permute(topk_ids: np.ndarray, E: int):
     return sorted_rows, offsets, m_indices
 
 
+def moe_align_block_size(topk_ids: np.ndarray, E: int, block_size: int):
+    """The block-padded layout of vLLM's moe_align_block_size with
+    ignore_invalid_experts=True, restated from its published description
+    (vllm/model_executor/layers/fused_moe/moe_align_block_size.py, the function
+    called at baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126), with the
+    stable order inside an expert: returns (sorted_ids, expert_ids, num_post_pad)."""
+    flat = np.asarray(topk_ids, np.int64).reshape(-1)
+    numel = flat.size
+    max_padded = numel + E * (block_size - 1)
+    if numel < E:
+        max_padded = min(max_padded, numel * block_size)
+    max_blocks = -(-max_padded // block_size)
+    sorted_ids = np.full(max_padded, numel, np.int32)
+    expert_ids = np.full(max_blocks, -1, np.int32)
+    p = 0
+    for e in range(E):
+        idx = np.nonzero(flat == e)[0]
+        n = -(-idx.size // block_size) * block_size
+        sorted_ids[p:p + idx.size] = idx
+        expert_ids[p // block_size:(p + n) // block_size] = e
+        p += n
+    return sorted_ids, expert_ids, np.array([p], np.int32)
+
+
 def quant_act_fp8_1x128(x_bf16: np.ndarray, gather_rows: np.ndarray | None = None,
                         gather_div: int = 1, R: int | None = None):
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)

@@ -147,3 +147,14 @@ def test_fast_and_scalar_int4_oracles_agree():
 def test_rel_err_counts_nan():
     r = O.rel_err(np.array([1.0, np.nan]), np.array([1.0, 2.0]))
     assert r["nan"] == 1 and r["max_rel"] == np.inf
+
+
+def test_align_block_size_oracle_layout():
+    """Padded layout: each expert's ascending flat indices, padded with
+    T*topk to the block size; blocks carry their expert, -1 past the end."""
+    ids = np.array([[1, 0], [1, 2], [0, 5], [1, 1]], np.int32)    # 5 is invalid with E=3
+    s, e, n = O.moe_align_block_size(ids, 3, 4)
+    assert n.tolist() == [12]
+    assert s[:12].tolist() == [1, 4, 8, 8, 0, 2, 6, 7, 3, 8, 8, 8]
+    assert e.tolist()[:3] == [0, 1, 2] and all(v == -1 for v in e.tolist()[3:])
+    assert len(s) == 8 + 3 * 3 and (s[12:] == 8).all()
