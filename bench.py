@@ -119,7 +119,9 @@ class Clocks:
 
 
 def fp8_algorithmic(cfg, counts):
-    """SURVEY-defined algorithmic bytes and FLOPs for the FP8 W13 GEMM."""
+    """Algorithmic bytes and FLOPs of the FP8 W13 GEMM: every active expert's
+    weights and block scales read once, activations and their scales read once,
+    outputs written once; FLOPs 2*R*N*K over real rows (decode.yaml:100)."""
     R = int(sum(counts))
     active = sum(1 for c in counts if c > 0)
     n_out = cfg.N // 2 if cfg.silu else cfg.N
@@ -131,8 +133,9 @@ def fp8_algorithmic(cfg, counts):
 
 
 def int4_algorithmic(cfg, counts):
-    """SURVEY-defined algorithmic bytes and FLOPs for the INT4 W13 GEMM, and the
-    reference's narrower INT4 weight bytes (baseline_marlin.py:204-206)."""
+    """Algorithmic bytes and FLOPs of the INT4 W13 GEMM (packed weights and
+    group scales of every active expert once, activations once, outputs once),
+    and the reference's narrower INT4 weight bytes (baseline_marlin.py:204-206)."""
     R = int(sum(counts))
     active = sum(1 for c in counts if c > 0)
     n_out = cfg.N // 2 if cfg.silu else cfg.N

@@ -47,6 +47,7 @@ SIGNATURES = {
     "ferret_int4_moe_w13": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous_noalloc": (
         _i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "ferret_moe_combine": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "ferret_ep_handle_bytes": (_sz, []),
     "ferret_ep_init": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _p, _p, ctypes.POINTER(_p)]),
     "ferret_ep_connect": (_i, [_p, _p]),

@@ -257,6 +257,47 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
     return bufs.out, bufs.sorted_rows, bufs.offsets
 
 
+def moe_combine(y: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor | None = None,
+                num_experts: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = sum_j topk_weights[t, j] * y[t*topk + j] (fp32, slot order, bf16 out);
+    pairs whose id is outside [0, num_experts) are skipped when topk_ids is given."""
+    _need(y, torch.bfloat16, "y", 2)
+    _need(topk_weights, torch.float32, "topk_weights", 2)
+    T, topk = topk_weights.shape
+    H = y.shape[1]
+    if y.shape[0] != T * topk:
+        raise ValueError("y must hold T*topk rows")
+    if topk_ids is not None:
+        _need(topk_ids, torch.int32, "topk_ids", 2)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
+    check(lib().ferret_moe_combine(_ptr(y), _ptr(topk_weights), _ptr(topk_ids), num_experts, T,
+                                   topk, H, _ptr(out), _stream()), "ferret_moe_combine")
+    return out
+
+
+def fp8_moe_ffn(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                W13: torch.Tensor, W13_scale: torch.Tensor, W2: torch.Tensor,
+                W2_scale: torch.Tensor) -> torch.Tensor:
+    """The FP8 MoE expert layer on one GPU: permute -> 1x128 quant -> W13 grouped
+    GEMM with fused SiLU(gate)*up -> 1x128 quant of the intermediate -> W2
+    grouped GEMM writing (token, slot) order -> top-k weighted combine.
+
+    hidden bf16 [T, H]; topk_ids int32 / topk_weights f32 [T, topk];
+    W13 e4m3 [E, 2I, H] + scales [E, 2I/128, H/128]; W2 e4m3 [E, H, I] + scales
+    [E, H/128, I/128].  Returns bf16 [T, H]."""
+    T, H = hidden.shape
+    topk = topk_ids.shape[1]
+    E, N13, _ = W13.shape
+    if W2.shape[0] != E or W2.shape[1] != H or W2.shape[2] != N13 // 2:
+        raise ValueError("W2 must be [E, H, I] with I = W13.shape[1] / 2")
+    y1, rows, offs = fp8_moe_w13(hidden, topk_ids, W13, W13_scale, silu=True)
+    q2, s2 = per_token_cast_to_fp8(y1)
+    y2 = torch.empty(T * topk, H, dtype=torch.bfloat16, device=hidden.device)
+    m_grouped_fp8_gemm_scatter((q2, s2), (W2, W2_scale), y2, offs, rows)
+    return moe_combine(y2, topk_weights, topk_ids, E)
+
+
 # ---------------------------------------------------------------- INT4 W4A16
 
 class Int4W13Weights:

@@ -241,6 +241,20 @@ FERRET_API int ferret_int4_repack_w13(const int32_t* w_raw, const void* w_scale_
                                       int E, int K, int N, void* stream);
 
 /*
+ * Top-k weighted combine after the W2 (down) projection -- the step that
+ * completes the MoE layer.  No reference counterpart: the reference times the
+ * grouped GEMMs alone (its W2 shapes: tasks/fp8-group-gemm-dsv3-decode.yaml:67-86).
+ * out[t, h] = bf16(sum_j w[t, j] * y[t*topk + j, h]), fp32 in slot order,
+ * pairs whose topk_ids entry is outside [0, E) skipped (topk_ids may be NULL:
+ * every pair counts).  y_bf16 [T*topk, H] in (token, slot) order -- the
+ * scatter grouped GEMM with out_rows = sorted_rows writes it so;
+ * topk_weights f32 [T, topk]; out_bf16 [T, H].  Limits: H % 8 == 0.
+ */
+FERRET_API int ferret_moe_combine(const void* y_bf16, const float* topk_weights,
+                                  const int32_t* topk_ids, int E, int T, int topk, int H,
+                                  void* out_bf16, void* stream);
+
+/*
  * INT4 W4A16 grouped GEMM for the W13 projection (group-32 symmetric bf16
  * scales, offset-8 nibbles), optional fused SiLU(gate)*up.
  * Replaces: vLLM ops.moe_wna16_marlin_gemm(...) followed by

@@ -348,3 +348,29 @@ def int4_w13_torch_cpu(x_bf16, raw_e, scales_e, silu=True):
         g, u = acc[:, : N // 2], acc[:, N // 2:]
         acc = g / (1.0 + torch.exp(-g)) * u
     return acc
+
+
+def fp8_moe_ffn(hidden_bf16, topk_ids, topk_weights, w13, w13_s, w2, w2_s):
+    """The FP8 MoE expert layer restated for the CPU: per (token, slot) pair,
+    1x128 quant -> W13 (fp32, exact block scales) -> SiLU(gate)*up -> bf16 ->
+    1x128 quant -> W2 -> bf16; then the fp32 top-k weighted sum in slot order
+    -> bf16.  Pairs with an id outside [0, E) are skipped.  Returns fp32 values
+    of the bf16 result, [T, H]."""
+    T, H = hidden_bf16.shape
+    topk = topk_ids.shape[1]
+    E = w13.shape[0]
+    flat = np.asarray(topk_ids).reshape(-1)
+    pairs = np.nonzero((flat >= 0) & (flat < E))[0]
+    a = hidden_bf16[pairs // topk]
+    q1, s1 = quant_act_fp8_1x128(a)
+    y1 = fp8_grouped_gemm_fast(q1, s1, w13, w13_s, flat[pairs].astype(np.int32), silu=True)
+    y1 = f32_to_bf16(y1)
+    q2, s2 = quant_act_fp8_1x128(y1)
+    y2 = bf16_to_f32(f32_to_bf16(fp8_grouped_gemm_fast(q2, s2, w2, w2_s, flat[pairs].astype(np.int32))))
+    out = np.zeros((T, H), np.float32)
+    w = np.asarray(topk_weights, np.float32).reshape(-1)
+    for j in range(topk):                      # slot order, as the device sums
+        sel = np.nonzero(pairs % topk == j)[0]
+        t = pairs[sel] // topk
+        out[t] = out[t] + w[pairs[sel]][:, None] * y2[sel]
+    return bf16_to_f32(f32_to_bf16(out))

@@ -53,8 +53,11 @@ def test_align_block_size_matches_vllm_sets(ops):
             pytest.skip(f"vLLM op failed to run: {type(exc).__name__}")
         s, e, n = ops.moe_align_block_size(ids, bs, E)
         total = int(n.item())
-        assert total == int(vn.item())
-        assert np.array_equal(e.cpu().numpy()[: total // bs], ve.cpu().numpy()[: total // bs])
+        assert total == int(vn.item()), (T, total, int(vn.item()))
+        e, ve = e.cpu().numpy(), ve.cpu().numpy()
+        assert len(e) == len(ve) and len(s) == len(vs), (len(e), len(ve), len(s), len(vs))
+        assert np.array_equal(e[: total // bs], ve[: total // bs]), (T, e[:8], ve[:8])
         s, vs = s.cpu().numpy(), vs.cpu().numpy()
         for b in range(total // bs):          # same set of pairs in every block
-            assert set(s[b * bs:(b + 1) * bs]) == set(vs[b * bs:(b + 1) * bs])
+            assert set(s[b * bs:(b + 1) * bs]) == set(vs[b * bs:(b + 1) * bs]), (
+                T, b, s[b * bs:(b + 1) * bs], vs[b * bs:(b + 1) * bs])
