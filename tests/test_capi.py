@@ -100,3 +100,44 @@ def test_ops_import_fails_loudly_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "_LIB", None)
     with pytest.raises(ImportError, match="not found"):
         _lib.lib()
+
+
+def test_align_block_size_sizes_follow_vllm_formula(L):
+    """Buffer sizes of vLLM's moe_align_block_size: numel + E*(bs-1), capped at
+    numel*bs when numel < E; blocks = ceil(size / bs)."""
+    mp, mb = ctypes.c_int(0), ctypes.c_int(0)
+    for T, topk, E, bs in ((64, 8, 384, 16), (1, 8, 384, 16), (4, 3, 4, 4), (7, 2, 5, 1)):
+        assert L.ferret_moe_align_block_size_sizes(T, topk, E, bs, ctypes.byref(mp),
+                                                   ctypes.byref(mb)) == 0
+        numel = T * topk
+        want = numel + E * (bs - 1)
+        if numel < E:
+            want = min(want, numel * bs)
+        assert mp.value == want and mb.value == -(-want // bs)
+    assert L.ferret_moe_align_block_size_sizes(4, 2, 8, 0, ctypes.byref(mp), ctypes.byref(mb)) == -1
+    f = L.ferret_moe_align_block_size
+    assert f(P, 4, 2, 8, 16, P, P, P, None, 0, None) == -7          # workspace missing
+    assert f(P, 4, 2, 2048, 16, P, P, P, P, 1 << 20, None) == -1     # E beyond the sort's limit
+
+
+def test_combine_and_ep_validation(L):
+    c = L.ferret_moe_combine
+    assert c(P, P, None, 0, 4, 2, 100, P, None) == -1                # H % 8
+    assert c(P, P, P, 0, 4, 2, 128, P, None) == -1                   # ids without E
+    assert c(None, P, None, 0, 4, 2, 128, P, None) == -3
+    assert c(ctypes.c_void_p(0x1008), P, None, 0, 4, 2, 128, P, None) == -2
+    assert c(P, P, None, 0, 0, 2, 128, P, None) == 0                  # no tokens: no-op
+    ctx = ctypes.c_void_p()
+    h = (ctypes.c_uint8 * int(L.ferret_ep_handle_bytes()))()
+    init = L.ferret_ep_init
+    args = lambda **kw: dict(dict(rank=0, world=2, E=256, topk=8, T=64, K=7168, N=4096, flags=0), **kw)
+    for bad in (dict(world=9), dict(rank=2), dict(E=255), dict(K=7000), dict(flags=1, N=4224),
+                dict(T=0)):
+        a = args(**bad)
+        assert init(a["rank"], a["world"], a["E"], a["topk"], a["T"], a["K"], a["N"], a["flags"],
+                    None, ctypes.cast(h, ctypes.c_void_p), ctypes.byref(ctx)) == -1, bad
+    assert init(0, 2, 256, 8, 64, 7168, 4096, 0, None, None, ctypes.byref(ctx)) == -3
+    assert L.ferret_ep_connect(None, P) == -3
+    assert L.ferret_ep_w13_forward(None, P, P, 1, P, P, P, None) == -3
+    assert L.ferret_ep_destroy(None) == -3
+    assert L.ferret_ep_output_buffer(None) is None
