@@ -69,97 +69,56 @@ def peaks():
 
 
 class Clocks:
-    """SM clock and clock-event-reason sampler running during the timed region:
-    NVML polled every 20 ms from a thread (falls back to `nvidia-smi -lms 200`).
-    Only reads settings.  (A 2 ms poll coincided with a 14 % slower prefill
-    GEMM on one run, so the poll stays sparse.)"""
+    """nvidia-smi sampler (a separate process, 100 ms interval) running during the
+    timed region.  An in-process NVML polling thread was tried and dropped: it
+    coincided with 10-14 % slower timed GEMMs (host-side contention in the
+    launch loop)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.path = None
-        self.thread = None
-        self.rows = []
-
-    def _nvml_handle(self):
-        import pynvml
-        pynvml.nvmlInit()
-        try:
-            import torch
-            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
-            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-        except Exception:
-            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
-        try:
-            import threading
-
-            import pynvml
-            h = self._nvml_handle()
-            bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
-                    pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
-            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
-            self.stop_flag = False
-
-            def poll():
-                while not self.stop_flag:
-                    try:
-                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                        self.rows.append((sm, mx, ["Active" if rs & b else "Not Active" for b in bits]))
-                    except Exception:
-                        pass
-                    time.sleep(0.02)
-            self.thread = threading.Thread(target=poll, daemon=True)
-            self.thread.start()
-            return
-        except Exception:
-            self.thread = None
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
 
     def stop(self):
-        rows = self.rows
-        if self.thread is not None:
-            self.stop_flag = True
-            self.thread.join(timeout=2)
-        elif self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            for line in open(self.path):
-                f = [x.strip() for x in line.split(",")]
-                if len(f) < 9:
-                    continue
-                try:
-                    rows.append((float(f[1]), float(f[2]), f[5:9]))
-                except ValueError:
-                    continue
-            os.unlink(self.path)
-        else:
+        if self.proc is None:
             return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
         if not rows:
             return None
-        reasons = sorted({n for _, _, fl in rows for n, v in zip(self.NAMES, fl) if v.lower() == "active"})
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for _, _, fl in rows for n, v in zip(names, fl) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows),
-                "sampler": "nvml 20 ms" if self.thread is not None else "nvidia-smi 200 ms"}
+                "reasons": reasons, "samples": len(rows), "sampler": "nvidia-smi 100 ms"}
 
 
 def fp8_algorithmic(cfg, counts):
