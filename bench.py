@@ -70,9 +70,9 @@ def peaks():
 
 class Clocks:
     """nvidia-smi sampler (a separate process, 100 ms interval) running during the
-    timed region.  An in-process NVML polling thread was tried and dropped: it
-    coincided with 10-14 % slower timed GEMMs (host-side contention in the
-    launch loop)."""
+    timed region.  An in-process NVML polling thread was tried and dropped: with
+    it the timed GEMMs read 2-13 % slower than the same launches timed without
+    it (cause not isolated)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
