@@ -12,9 +12,11 @@
 //     TMA boxes, however few tokens an expert has (decode).
 //   * warp 0 streams W and A tiles with TMA into an NS-deep shared-memory
 //     ring (128-byte swizzle); weights carry an evict-first L2 hint.
-//   * warp 1 issues tcgen05.mma kind::f8f6f4 (M=128, N=NT, K=32) from one
-//     elected thread; each 128-wide K block goes to its own TMEM accumulator
-//     buffer (up to 8 in flight) so the scales can be applied exactly.
+//   * warp 1 issues tcgen05.mma kind::f8f6f4 (M=128, K=32, N = the tile's
+//     live token rows rounded up to 16) from one elected thread; each 128-wide
+//     K block goes to its own TMEM accumulator buffer (up to 8 in flight) so
+//     the scales can be applied exactly.  Activation rows arrive in 16-row
+//     TMA boxes, only as many as the tile holds.
 //   * warps 2-5 (128 threads, one TMEM lane = one weight row each) read each
 //     K-block partial with tcgen05.ld and promote it in fp32 registers:
 //     acc += partial * (a_scale * w_scale) -- the exact-fp32-scale contract
@@ -24,7 +26,11 @@
 //   * tiles never straddle experts: the schedule is built per CTA in the
 //     prologue from the expert segments (prefix offsets, or (start, count)
 //     pairs derived from m_indices), so ragged groups of any size are exact.
+//   * when the tiles cannot fill half the SMs, K is split over them: fp32
+//     partials in the workspace, reduced in split order by the last unit of
+//     each tile (an atomic tile counter) -- deterministic.
 // Every mbarrier wait is bounded (ferret_common.cuh).
+// The prefill-shaped kernel (tokens on MMA M) follows further below.
 #include <algorithm>
 
 #include "capi_internal.h"

@@ -30,6 +30,11 @@
 //     accumulating the whole K range in one TMEM buffer per tile
 //     (double-buffered across tiles);
 //   * warps 18-21 (epilogue): TMEM -> registers -> optional SiLU*up -> bf16.
+// A dequant warp leaves a tile's TMEM stores in flight while it dequantizes
+// its next tile, and only then hands the slot to the MMA.  With fewer tiles
+// than SMs (a handful of tokens) the K blocks are split over the SMs; fp32
+// partials go to the workspace and the last unit of each tile reduces them
+// in split order (deterministic).
 // The dequant arithmetic is exact: nibble pairs become bf16 (128 + n) with one
 // lop3 against the 0x4300 exponent, minus 136 gives n - 8 exactly, and one
 // bf16x2 multiply by the scale rounds once -- the oracle's bf16((n-8)*s).
@@ -40,7 +45,7 @@
 namespace ferret {
 namespace {
 
-constexpr int kDqWarp0 = 2, kDqWarps = 16, kDqThreads = kDqWarps * 32;
+constexpr int kDqWarp0 = 2, kDqWarps = 16;
 constexpr int kEpiWarp0 = kDqWarp0 + kDqWarps, kI4EpiThreads = 128;
 constexpr int kI4Threads = (kEpiWarp0 + 4) * 32;   // 22 warps
 constexpr int kI4MaxE = 1024;
