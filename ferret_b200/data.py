@@ -35,7 +35,7 @@ class W13Config:
         return self.T * self.topk
 
 
-# The workload configurations
+# The workload configurations (the five benchmark configurations, numbered 1-5)
 CONFIGS = {
     "cpu_fp8": W13Config("cpu_fp8", E=8, topk=2, T=256, K=512, N=1024),
     "dsv3_decode": W13Config("dsv3_decode", E=256, topk=8, T=128, K=7168, N=4096),

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference tree (read-only) and its toolchain:
 
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 It writes, next to this script:
 

@@ -299,7 +299,7 @@ def oracle_w13(hidden, ids, w, w_s, E, silu):
 
 @pytest.mark.parametrize("silu", [False, True])
 def test_w13_path_cpu_config(ops, silu):
-    """BASELINE config 1 (E=8, top-2 uniform, 256 tokens, K=512, N=1024), all rows."""
+    """Benchmark configuration 1 (E=8, top-2 uniform, 256 tokens, K=512, N=1024), all rows."""
     from ferret_b200 import data
     cfg = data.CONFIGS["cpu_fp8"]
     W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K)
@@ -315,7 +315,7 @@ def test_w13_path_cpu_config(ops, silu):
 
 
 def test_w13_path_dsv3_decode_full_size(ops):
-    """BASELINE config 2 at full size; every output row of 48 sampled experts
+    """Benchmark configuration 2 at full size; every output row of 48 sampled experts
     is checked against the fp32 oracle, permutation and quantization in full."""
     from ferret_b200 import data
     cfg = data.CONFIGS["dsv3_decode"]
@@ -366,7 +366,7 @@ def test_ep_single_rank_matches_w13_path(ops):
 
 
 def test_w13_path_dsv3_prefill_full_size(ops):
-    """BASELINE config 3 (E=256, top-8 Zipf(1.1), 8192 tokens) at full size, plain
+    """Benchmark configuration 3 (E=256, top-8 Zipf(1.1), 8192 tokens) at full size, plain
     and fused SiLU: every row of 6 sampled experts (the largest among them)
     against the fp32 oracle."""
     from ferret_b200 import data

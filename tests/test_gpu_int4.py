@@ -136,7 +136,7 @@ def test_int4_reference_distribution_max_abs(ops, T):
 
 
 def test_int4_kimi_decode_full_size(ops):
-    """BASELINE config 4 at full size (E=384, top-8, 64 tokens, K=7168, N=4096),
+    """Benchmark configuration 4 at full size (E=384, top-8, 64 tokens, K=7168, N=4096),
     plain and SiLU outputs; all pairs of 40 sampled experts checked."""
     from ferret_b200 import data
     cfg = data.CONFIGS["kimi_int4_decode"]
