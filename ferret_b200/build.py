@@ -6,7 +6,8 @@ Each ``csrc/*.cu`` is compiled by nvcc into ``_build/`` (in parallel) and the
 objects are linked into one shared library with the CUDA runtime linked
 statically, so the library loads on machines without a GPU driver (the
 driver-API entry point the TMA descriptors need is resolved at run time
-through the runtime).
+through the runtime).  ``kernel_result.cu`` becomes the benchmark binary
+``ferret_b200/ferret_kernel_result`` linked against that library.
 """
 from __future__ import annotations
 
@@ -21,6 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libferret_moe.so")
+BIN = os.path.join(HERE, "ferret_kernel_result")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -41,7 +43,8 @@ def _sources():
 
 def _deps():
     return [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [
-        os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)]
+        os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)] + [
+        os.path.join(HERE, "kernel_result.cu")]
 
 
 def _stale(target, deps):
@@ -55,7 +58,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     os.makedirs(BUILD, exist_ok=True)
     srcs = _sources()
     deps = _deps()
-    if not force and not _stale(LIB, deps + [__file__]):
+    if not force and not _stale(LIB, deps + [__file__]) and not _stale(BIN, deps + [__file__]):
         return LIB
     cc = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
@@ -85,7 +88,22 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
+    build_kernel_result(cc, verbose)
     return LIB
+
+
+def build_kernel_result(cc: str, verbose: bool = False) -> str:
+    """The self-contained benchmark binary (KERNEL_RESULT lines), linked
+    against the library next to it."""
+    src = os.path.join(HERE, "kernel_result.cu")
+    cmd = [cc, *ARCH, "-O2", "-std=c++17", src, "-o", BIN, "-L", HERE, "-lferret_moe",
+           "-Xlinker", "-rpath,$ORIGIN", "-cudart", "static"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"kernel_result build failed:\n{r.stdout}\n{r.stderr}")
+    return BIN
 
 
 def main():

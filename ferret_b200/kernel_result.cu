@@ -1,0 +1,317 @@
+// kernel_result.cu -- self-contained benchmark binary in the reference's
+// result format: for every configuration of a task it builds seeded inputs,
+// runs the library through its C ABI, checks the output against a host fp32
+// reference, times the call and prints
+//
+//   KERNEL_RESULT {"<config>": <TFLOPS>, ...}
+//   KERNEL_RESULT_REFERENCE {}
+//
+// the line the reference's harness parses (task_spec.py:277-328); a config
+// whose check fails reports 0.0 and "INVALID" on stderr.  Tasks and shapes
+// are the reference's (tasks/fp8-group-gemm-dsv3-decode.yaml:45-86,
+// tasks/fp8-group-gemm-dsv3-prefill.yaml:54-95,
+// tasks/kimi-moe-w13-int4-grouped-gemm.yaml:135-138 plus T=1 of
+// baselines/kimi-moe-w13-int4/baseline_marlin.py).
+// Timing follows the reference: warm-up, then per iteration a 256 MB memset
+// flush of L2, CUDA events around the call, median.
+//
+//   usage: ferret_kernel_result [decode|prefill|kimi] [iterations]
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../include/ferret_moe.h"
+
+namespace {
+
+struct Rng {   // xorshift64*, seeded per config
+    uint64_t s;
+    explicit Rng(uint64_t seed) : s(seed * 0x9E3779B97F4A7C15ull + 1) {}
+    uint64_t next() {
+        s ^= s >> 12;
+        s ^= s << 25;
+        s ^= s >> 27;
+        return s * 0x2545F4914F6CDD1Dull;
+    }
+    float uni() { return (next() >> 40) * (1.0f / 16777216.0f); }   // [0, 1)
+    float normal() {
+        const float u1 = std::max(uni(), 1e-7f), u2 = uni();
+        return std::sqrt(-2.0f * std::log(u1)) * std::cos(6.2831853f * u2);
+    }
+};
+
+float e4m3_to_f32(uint8_t b) {
+    const int s = b >> 7, e = (b >> 3) & 15, m = b & 7;
+    float v = e == 0 ? std::ldexp((float)m, -9) : std::ldexp(1.0f + m / 8.0f, e - 7);
+    return s ? -v : v;
+}
+
+uint16_t f32_to_bf16(float f) {          // round to nearest even
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+float bf16_to_f32(uint16_t h) {
+    const uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+bool ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        std::fprintf(stderr, "CUDA error %s: %s\n", what, cudaGetErrorString(e));
+        return false;
+    }
+    return true;
+}
+
+// Median time in ms of `iters` calls, each after a 256 MB flush.
+template <typename F>
+float time_median(F&& call, void* flush, size_t flush_bytes, int iters, cudaStream_t s) {
+    for (int i = 0; i < 20; ++i) call();
+    cudaStreamSynchronize(s);
+    std::vector<float> t(iters);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    for (int i = 0; i < iters; ++i) {
+        cudaMemsetAsync(flush, 0, flush_bytes, s);
+        cudaEventRecord(a, s);
+        call();
+        cudaEventRecord(b, s);
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&t[i], a, b);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    std::sort(t.begin(), t.end());
+    return t[iters / 2];
+}
+
+struct Fp8Cfg { const char* name; int mpe, E, K, N; };
+
+// One FP8 grouped-GEMM configuration: DeepGEMM-style call with m_indices.
+double run_fp8(const Fp8Cfg& c, int iters, void* flush, size_t flush_bytes, cudaStream_t s,
+               int seed) {
+    const int M = c.mpe * c.E, K = c.K, N = c.N, E = c.E, nk = K / 128;
+    Rng r(seed);
+    std::vector<uint8_t> a((size_t)M * K), w((size_t)E * N * K);
+    for (auto& v : a) { v = (uint8_t)(r.next() % 254); if (v >= 0x7F) ++v; }   // no NaN codes
+    for (auto& v : w) { v = (uint8_t)(r.next() % 254); if (v >= 0x7F) ++v; }
+    std::vector<float> as((size_t)M * nk), ws((size_t)E * (N / 128) * nk);
+    for (auto& v : as) v = 0.5f + 0.5f * r.uni();
+    for (auto& v : ws) v = 0.5f + 0.5f * r.uni();
+    std::vector<int32_t> mi(M);
+    for (int i = 0; i < M; ++i) mi[i] = i / c.mpe;
+
+    void *da, *dw, *dout, *dws;
+    float *das, *dwsc;
+    int32_t* dmi;
+    const size_t wsb = ferret_fp8_grouped_gemm_workspace_size(M, E);
+    if (!ok(cudaMalloc(&da, a.size()), "alloc") || !ok(cudaMalloc(&dw, w.size()), "alloc") ||
+        !ok(cudaMalloc(&das, as.size() * 4), "alloc") || !ok(cudaMalloc(&dwsc, ws.size() * 4), "alloc") ||
+        !ok(cudaMalloc(&dout, (size_t)M * N * 2), "alloc") || !ok(cudaMalloc(&dmi, M * 4), "alloc") ||
+        !ok(cudaMalloc(&dws, std::max<size_t>(wsb, 256)), "alloc"))
+        return 0.0;
+    cudaMemcpy(da, a.data(), a.size(), cudaMemcpyHostToDevice);
+    cudaMemcpy(dw, w.data(), w.size(), cudaMemcpyHostToDevice);
+    cudaMemcpy(das, as.data(), as.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dwsc, ws.data(), ws.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dmi, mi.data(), M * 4, cudaMemcpyHostToDevice);
+    auto call = [&]() {
+        return ferret_fp8_grouped_gemm_nt_contiguous(da, das, dw, dwsc, dout, dmi, nullptr, M, N, K,
+                                                     E, 0, dws, wsb, s);
+    };
+    int rc = call();
+    cudaStreamSynchronize(s);
+    int32_t st = 0;
+    ferret_last_device_status(s, &st);
+    bool valid = rc == FERRET_OK && st == 0;
+
+    // host fp32 check (exact block scales, per-row experts) on up to 64 rows
+    std::vector<uint16_t> out((size_t)M * N);
+    cudaMemcpy(out.data(), dout, out.size() * 2, cudaMemcpyDeviceToHost);
+    std::vector<int> rows;
+    for (int i = 0; i < std::min(M, 32); ++i) rows.push_back(i);
+    for (int i = std::max(32, M - 32); i < M; ++i) rows.push_back(i);
+    double max_abs = 0.0, max_err = 0.0;
+    std::vector<double> ref(rows.size() * (size_t)N);
+    for (size_t ri = 0; ri < rows.size(); ++ri) {
+        const int m = rows[ri], e = mi[m];
+        for (int n = 0; n < N; ++n) {
+            double acc = 0.0;
+            for (int kb = 0; kb < nk; ++kb) {
+                double dot = 0.0;
+                const uint8_t* ar = &a[(size_t)m * K + kb * 128];
+                const uint8_t* wr = &w[((size_t)e * N + n) * K + kb * 128];
+                for (int k = 0; k < 128; ++k) dot += (double)e4m3_to_f32(ar[k]) * e4m3_to_f32(wr[k]);
+                acc += dot * as[(size_t)m * nk + kb] * ws[((size_t)e * (N / 128) + n / 128) * nk + kb];
+            }
+            ref[ri * N + n] = acc;
+            max_abs = std::max(max_abs, std::fabs(acc));
+        }
+    }
+    for (size_t ri = 0; ri < rows.size(); ++ri)
+        for (int n = 0; n < N; ++n) {
+            const double g = bf16_to_f32(out[(size_t)rows[ri] * N + n]), rv = ref[ri * N + n];
+            if (std::isnan(g)) { max_err = 1e30; continue; }
+            max_err = std::max(max_err, std::fabs(g - rv) / std::max(std::fabs(rv), 1e-3 * max_abs));
+        }
+    valid = valid && max_err < 1e-2;
+    double tflops = 0.0;
+    if (valid) {
+        const float ms = time_median(call, flush, flush_bytes, iters, s);
+        tflops = 2.0 * M * N * (double)K / (ms * 1e-3) / 1e12;
+        const double gbs = ((double)E * N * K + (double)M * K + (double)M * N * 2) / (ms * 1e-3) / 1e9;
+        std::fprintf(stderr, "%s: %.2f us, %.3f TFLOPS, %.0f GB/s, max rel err %.2e\n", c.name,
+                     ms * 1e3, tflops, gbs, max_err);
+    } else {
+        std::fprintf(stderr, "INVALID: %s (rc %d, status %d, max rel err %.2e)\n", c.name, rc, st,
+                     max_err);
+    }
+    cudaFree(da); cudaFree(dw); cudaFree(das); cudaFree(dwsc); cudaFree(dout); cudaFree(dmi);
+    cudaFree(dws);
+    return tflops;
+}
+
+// Kimi INT4 W13 with fused SiLU: T tokens, top-8 of E distinct experts each.
+double run_kimi(const char* name, int T, int iters, void* flush, size_t flush_bytes,
+                cudaStream_t s, int seed) {
+    const int topk = 8, K = 7168, N = 512, E = 384, R = T * topk, n_out = N / 2;
+    Rng r(seed);
+    std::vector<int32_t> raw((size_t)E * (K / 8) * N);
+    for (auto& v : raw) v = (int32_t)(r.next() >> 32);
+    std::vector<uint16_t> sc((size_t)E * (K / 32) * N), hid((size_t)T * K);
+    for (auto& v : sc) v = f32_to_bf16(std::fabs(r.normal()) * 0.01f);
+    for (auto& v : hid) v = f32_to_bf16(r.normal() * 0.01f);
+    std::vector<int32_t> ids(R);
+    for (int t = 0; t < T; ++t) {           // 8 distinct experts per token
+        std::vector<int> pool(E);
+        for (int e = 0; e < E; ++e) pool[e] = e;
+        for (int j = 0; j < topk; ++j) {
+            const int k = j + (int)(r.next() % (uint64_t)(E - j));
+            std::swap(pool[j], pool[k]);
+            ids[t * topk + j] = pool[j];
+        }
+    }
+    void *draw, *dsc, *dblob, *dhid, *dout, *dws;
+    int32_t *dids, *drows, *doffs, *dmi;
+    const size_t blob = ferret_int4_blob_bytes(E, K, N);
+    const size_t wsb = ferret_int4_moe_w13_workspace_size(T, topk, K);
+    if (!ok(cudaMalloc(&draw, raw.size() * 4), "alloc") || !ok(cudaMalloc(&dsc, sc.size() * 2), "alloc") ||
+        !ok(cudaMalloc(&dblob, blob), "alloc") || !ok(cudaMalloc(&dhid, hid.size() * 2), "alloc") ||
+        !ok(cudaMalloc(&dout, (size_t)R * n_out * 2), "alloc") || !ok(cudaMalloc(&dws, wsb), "alloc") ||
+        !ok(cudaMalloc(&dids, R * 4), "alloc") || !ok(cudaMalloc(&drows, R * 4), "alloc") ||
+        !ok(cudaMalloc(&doffs, (E + 1) * 4), "alloc") || !ok(cudaMalloc(&dmi, R * 4), "alloc"))
+        return 0.0;
+    cudaMemcpy(draw, raw.data(), raw.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dsc, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice);
+    cudaMemcpy(dhid, hid.data(), hid.size() * 2, cudaMemcpyHostToDevice);
+    cudaMemcpy(dids, ids.data(), R * 4, cudaMemcpyHostToDevice);
+    int rc = ferret_int4_repack_w13(static_cast<const int32_t*>(draw), dsc, dblob, E, K, N, s);
+    if (rc == FERRET_OK)   // routing, once (set-up, outside the timed call as in the reference)
+        rc = ferret_moe_permute(dids, T, topk, E, drows, doffs, dmi, nullptr, 0, s);
+    auto call = [&]() {
+        return ferret_int4_moe_w13(dhid, dblob, drows, doffs, dout, T, topk, N, K, E,
+                                   FERRET_SILU_MUL, dws, wsb, s);
+    };
+    if (rc == FERRET_OK) rc = call();
+    cudaStreamSynchronize(s);
+    int32_t st = 0;
+    ferret_last_device_status(s, &st);
+    bool valid = rc == FERRET_OK && st == 0;
+    // host reference: bf16((n-8)*s) weights, fp32 accumulate, SiLU(gate)*up
+    std::vector<uint16_t> out((size_t)R * n_out);
+    cudaMemcpy(out.data(), dout, out.size() * 2, cudaMemcpyDeviceToHost);
+    double max_ae = 0.0;
+    std::vector<float> acc(N);
+    for (int p = 0; p < R; ++p) {
+        const int e = ids[p], t = p / topk;
+        std::fill(acc.begin(), acc.end(), 0.0f);
+        for (int k8 = 0; k8 < K / 8; ++k8)
+            for (int n = 0; n < N; ++n) {
+                const uint32_t word = (uint32_t)raw[((size_t)e * (K / 8) + k8) * N + n];
+                for (int q = 0; q < 8; ++q) {
+                    const int k = k8 * 8 + q;
+                    const float scale = bf16_to_f32(sc[((size_t)e * (K / 32) + k / 32) * N + n]);
+                    const float wv = bf16_to_f32(f32_to_bf16((float)((int)((word >> (4 * q)) & 15u) - 8) * scale));
+                    acc[n] += bf16_to_f32(hid[(size_t)t * K + k]) * wv;
+                }
+            }
+        for (int j = 0; j < n_out; ++j) {
+            const float g = acc[j], u = acc[n_out + j];
+            const float ref = bf16_to_f32(f32_to_bf16(g / (1.0f + std::exp(-g)) * u));
+            const float got = bf16_to_f32(out[(size_t)p * n_out + j]);
+            max_ae = std::isnan(got) ? 1e30 : std::max(max_ae, (double)std::fabs(got - ref));
+        }
+    }
+    valid = valid && max_ae < 0.012;
+    double tflops = 0.0;
+    if (valid) {
+        const float ms = time_median(call, flush, flush_bytes, iters, s);
+        tflops = 2.0 * R * N * (double)K / (ms * 1e-3) / 1e12;
+        std::vector<char> act(E, 0);
+        for (int v : ids) act[v] = 1;
+        const double nact = std::count(act.begin(), act.end(), 1);
+        std::fprintf(stderr, "%s: %.2f us, %.3f TFLOPS, INT4 weight %.3f TB/s, max abs err %.4f\n",
+                     name, ms * 1e3, tflops, nact * N * K * 0.5 / (ms * 1e-3) / 1e12, max_ae);
+    } else {
+        std::fprintf(stderr, "INVALID: %s (rc %d, status %d, max abs err %.4f)\n", name, rc, st, max_ae);
+    }
+    cudaFree(draw); cudaFree(dsc); cudaFree(dblob); cudaFree(dhid); cudaFree(dout); cudaFree(dws);
+    cudaFree(dids); cudaFree(drows); cudaFree(doffs); cudaFree(dmi);
+    return tflops;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    const std::string task = argc > 1 ? argv[1] : "decode";
+    const int iters = argc > 2 ? std::max(5, std::atoi(argv[2])) : 100;
+    static const Fp8Cfg decode[] = {
+        {"gate_up_M1", 1, 32, 7168, 4096}, {"gate_up_M4", 4, 32, 7168, 4096},
+        {"gate_up_M8", 8, 32, 7168, 4096}, {"gate_up_M16", 16, 32, 7168, 4096},
+        {"down_M1", 1, 32, 2048, 7168},    {"down_M4", 4, 32, 2048, 7168},
+        {"down_M8", 8, 32, 2048, 7168},    {"down_M16", 16, 32, 2048, 7168}};
+    static const Fp8Cfg prefill[] = {
+        {"gate_up_M64", 64, 32, 7168, 4096},   {"gate_up_M128", 128, 32, 7168, 4096},
+        {"gate_up_M256", 256, 32, 7168, 4096}, {"gate_up_M512", 512, 32, 7168, 4096},
+        {"down_M64", 64, 32, 2048, 7168},      {"down_M128", 128, 32, 2048, 7168},
+        {"down_M256", 256, 32, 2048, 7168},    {"down_M512", 512, 32, 2048, 7168}};
+    if (task != "decode" && task != "prefill" && task != "kimi") {
+        std::fprintf(stderr, "usage: %s [decode|prefill|kimi] [iterations]\n", argv[0]);
+        return 2;
+    }
+    cudaStream_t s;
+    if (!ok(cudaStreamCreate(&s), "stream")) return 1;
+    const size_t flush_bytes = (size_t)256 << 20;
+    void* flush = nullptr;
+    if (!ok(cudaMalloc(&flush, flush_bytes), "flush")) return 1;
+    std::string line = "KERNEL_RESULT {";
+    auto add = [&](const char* name, double v) {
+        char buf[128];
+        std::snprintf(buf, sizeof(buf), "%s\"%s\": %.4f", line.size() > 15 ? ", " : "", name, v);
+        line += buf;
+    };
+    if (task == "kimi") {
+        add("T1", run_kimi("T1", 1, iters, flush, flush_bytes, s, 1));
+        add("T8", run_kimi("T8", 8, iters, flush, flush_bytes, s, 8));
+    } else {
+        const Fp8Cfg* cfgs = task == "decode" ? decode : prefill;
+        for (int i = 0; i < 8; ++i) add(cfgs[i].name, run_fp8(cfgs[i], iters, flush, flush_bytes, s, 42 + i));
+    }
+    std::printf("%s}\nKERNEL_RESULT_REFERENCE {}\n", line.c_str());
+    cudaFree(flush);
+    cudaStreamDestroy(s);
+    return 0;
+}
