@@ -17,7 +17,8 @@ of the baselines it replaces:
 * ``ferret_moe::int4_moe_w13(Tensor hidden, Tensor w_raw, Tensor w_scale,
   Tensor topk_ids, bool silu=True) -> Tensor`` -- the raw compressed-tensors
   INT4 weights ([E, K/8, N] int32, [E, K/32, N] bf16), repacked once per
-  weight tensor and cached, then moe_wna16_marlin_gemm + SiLU
+  weight tensor pair (the last pair is cached, by identity and version), then
+  moe_wna16_marlin_gemm + SiLU
   (baseline_marlin.py:140-168).
 
 Every operator runs the CUDA library (CUDA tensors only); importing this
@@ -38,8 +39,9 @@ _LIB.define("moe_align_block_size(Tensor topk_ids, int block_size, int num_exper
 _LIB.define("int4_moe_w13(Tensor hidden, Tensor w_raw, Tensor w_scale, Tensor topk_ids, "
             "bool silu=True) -> Tensor")
 
-# repacked INT4 weights, keyed by the raw tensors' storage and version
-_INT4_CACHE: dict = {}
+# the last repacked INT4 weight set: (w_raw, w_scale, their versions, blob);
+# holding the raw tensors keeps their memory from being reused by others
+_INT4_CACHE: list = []
 
 
 def _fp8_gemm(a, a_scale, w, w_scale, out, m_indices, silu=False):
@@ -55,12 +57,14 @@ def _align(topk_ids, block_size, num_experts):
 
 
 def _int4(hidden, w_raw, w_scale, topk_ids, silu=True):
-    key = (w_raw.data_ptr(), w_raw._version, w_scale.data_ptr(), w_scale._version)
-    packed = _INT4_CACHE.get(key)
-    if packed is None:
-        packed = ops.Int4W13Weights(w_raw, w_scale)
+    versions = (w_raw._version, w_scale._version)
+    if (_INT4_CACHE and _INT4_CACHE[0] is w_raw and _INT4_CACHE[1] is w_scale
+            and _INT4_CACHE[2] == versions):
+        packed = _INT4_CACHE[3]
+    else:
         _INT4_CACHE.clear()          # one weight set at a time: repacks are GBs
-        _INT4_CACHE[key] = packed
+        packed = ops.Int4W13Weights(w_raw, w_scale)
+        _INT4_CACHE.extend([w_raw, w_scale, versions, packed])
     return ops.moe_wna16_w13(hidden, packed, topk_ids, silu=silu)
 
 
