@@ -52,6 +52,10 @@ def parse_args():
                     help="v007-configs: the reference kernel's own 8 benchmark shapes "
                          "(E=32 experts, gate_up and down, 1-16 rows per expert); with --impl "
                          "reference, the reference's own GPU kernel compiled unmodified")
+    ap.add_argument("--scales", choices=["fp32", "ue8m0"], default="fp32",
+                    help="FP8 block scales: fp32 (exact, the reference contract) or ue8m0 "
+                         "(power-of-two weights and activations; the 128-row-tile GEMM applies "
+                         "them inside the MMA, kind::mxf8f6f4.block_scale)")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="profiling aid: run N bare GEMM launches and exit")
     return ap.parse_args()
@@ -272,20 +276,25 @@ def run_single(args, cfg):
         return run_single_int4(args, cfg)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    W, W_s = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    ue8m0 = getattr(args, "scales", "fp32") == "ue8m0"
+    W, W_s = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev, use_ue8m0=ue8m0)
     hidden = data.activations(cfg.T, cfg.K).to(dev)
     ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
     n_out = cfg.N // 2 if cfg.silu else cfg.N
     bufs = ops.W13Buffers(cfg.T, cfg.topk, cfg.K, n_out, cfg.E, dev)
 
     def step():
-        ops.fp8_moe_w13(hidden, ids, W, W_s, silu=cfg.silu, bufs=bufs)
+        ops.fp8_moe_w13(hidden, ids, W, W_s, silu=cfg.silu, bufs=bufs, use_ue8m0=ue8m0)
+
+    def gemm():
+        ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
+                                             disable_ue8m0_cast=not ue8m0,
+                                             expert_offsets=bufs.offsets, silu=cfg.silu)
 
     if args.gemm_only:
         step()
         for _ in range(args.gemm_only):
-            ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
-                                                 expert_offsets=bufs.offsets, silu=cfg.silu)
+            gemm()
         torch.cuda.synchronize()
         return None
 
@@ -318,9 +327,6 @@ def run_single(args, cfg):
     torch.cuda.synchronize()
 
     # dominant kernel alone (same stream, same flush discipline)
-    def gemm():
-        ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
-                                             expert_offsets=bufs.offsets, silu=cfg.silu)
     gemm_ms = timed(graph_of(gemm).replay, args.steps)
 
     # end to end through the public API with host buffers
@@ -333,7 +339,8 @@ def run_single(args, cfg):
     def e2e():
         d_hidden.copy_(h_hidden, non_blocking=True)
         d_ids.copy_(h_ids, non_blocking=True)
-        out, _, _ = ops.fp8_moe_w13(d_hidden, d_ids, W, W_s, silu=cfg.silu, bufs=bufs)
+        out, _, _ = ops.fp8_moe_w13(d_hidden, d_ids, W, W_s, silu=cfg.silu, bufs=bufs,
+                                    use_ue8m0=ue8m0)
         h_out.copy_(out, non_blocking=True)
     e2e()
     e2e_ms = timed(e2e, args.steps)
@@ -350,7 +357,9 @@ def run_single(args, cfg):
     pk = peaks()
     # the library runs the prefill kernel when experts average more than 48 rows
     prefill = (cfg.R + cfg.E - 1) // cfg.E > 48 and cfg.N % 256 == 0
-    rl = roofline(byts, flops, g_ms, pk, "fp8_w13_prefill_kernel" if prefill else "fp8_w13_grouped_kernel")
+    kname = (("fp8_w13_prefill_mx_kernel" if ue8m0 else "fp8_w13_prefill_kernel") if prefill
+             else "fp8_w13_grouped_kernel")
+    rl = roofline(byts, flops, g_ms, pk, kname)
     res = {
         "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
         "value": round(flops / (ms * 1e-3) / 1e12, 3),
@@ -367,6 +376,7 @@ def run_single(args, cfg):
         "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
                    "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
+                   "scales": "ue8m0 (powers of two)" if ue8m0 else "fp32 (exact)",
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "hbm_gbs_step": round(byts / (ms * 1e-3) / 1e9, 1),
         "roofline": dict(rl, traffic=read_traffic(f"{rl['kernel'].removesuffix('_kernel')}_{cfg.name}")),
@@ -470,6 +480,7 @@ def run_single_int4(args, cfg):
         "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
                    "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
+                   "scales": "ue8m0 (powers of two)" if ue8m0 else "fp32 (exact)",
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "int4_weight_tbs": round(wbytes / (g_ms * 1e-3) / 1e12, 3),
         "roofline": {"bound": "hbm", "kernel": "int4_w13_grouped_kernel",

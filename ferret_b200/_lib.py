@@ -17,6 +17,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "ferret_moe.h")
 
 FERRET_SILU_MUL = 0x1
 FERRET_TILE_SHIFT = 8
+FERRET_UE8M0_SCALES = 0x2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -35,6 +36,7 @@ SIGNATURES = {
     "ferret_moe_align_block_size_workspace_size": (_sz, [_i, _i, _i]),
     "ferret_moe_align_block_size": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "ferret_quant_act_fp8_1x128": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+    "ferret_quant_act_fp8_1x128_ue8m0": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_gather_rows": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _sz, _p]),

@@ -240,6 +240,21 @@ __device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t adesc, uint
         : "memory");
 }
 
+// D[tmem] (+)= (A[smem] * 2^sfa) * (B[smem] * 2^sfb)^T, e4m3 operands with
+// UE8M0 block scales read from Tensor Memory (one per row and per K=32 slice,
+// scale vector 1X), fp32 accumulate.
+__device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "setp.ne.b32 P, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], P;\n\t}" ::
+            "r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, f16/bf16 operands, fp32 accumulate.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -277,6 +292,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
+// 32 lanes x 4 / 8 columns of 32-bit registers -> TMEM.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2,
+                                         uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+                 "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                     taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                 "r"(r[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -299,6 +330,14 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t a_fmt, uint32_t b_fmt) {
     return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | ((uint32_t)(N >> 3) << 17) |
            ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor of the block-scaled kind::mxf8f6f4 MMA: e4m3 A and B
+// (formats 0), both K-major, UE8M0 scale factors (bit 23), scale-factor ids
+// (bits 4-5 for B, 29-30 for A: the byte of the 32-bit TMEM word) 0, K = 32.
+// The accumulator of this kind is always f32 (no D-format field).
+__host__ __device__ constexpr uint32_t make_idesc_mx(int M, int N) {
+    return ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24);
 }
 
 // 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread.

@@ -8,7 +8,8 @@
 // `448.0 / amax` as reciprocal-then-multiply), q = e4m3(fl(x * f)) with
 // round-to-nearest-even and saturation, scale = fl(amax / 448).  Every step is
 // IEEE round-to-nearest (no fast-math), so the result is bit-identical to the
-// CPU restatement.
+// CPU restatement.  The UE8M0 form (use_ue8m0=True) rounds the scale up to a
+// power of two and multiplies by its exact inverse.
 //
 // HBM-bound: a warp quantizes 4 blocks of a row per task, 16 bytes per lane in.
 #include "capi_internal.h"
@@ -26,6 +27,9 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 // covers one block with 16-byte loads; both loads of a lane are issued before
 // either is used, so 1 KB per warp is in flight (the kernel is bound by the
 // latency of the gathered row reads, not by HBM, at decode sizes).
+// UE8M0: the scale is the smallest power of two >= fl(amax / 448), taken from
+// the fp32 bits (exact; no log2), and x is multiplied by its exact inverse.
+template <bool UE8M0>
 __global__ void __launch_bounds__(kQuantThreads)
     quant_act_kernel(const __nv_bfloat16* __restrict__ x, int x_rows,
                      const int32_t* __restrict__ gather, int gather_div, int R, int K,
@@ -76,8 +80,18 @@ __global__ void __launch_bounds__(kQuantThreads)
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
             if (b >= nk) continue;
             amax = fmaxf(amax, 1e-4f);
-            // `448.0 / amax` in the published torch code is reciprocal-then-multiply
-            const float f = __fmul_rn(__frcp_rn(amax), 448.0f);
+            float f, sc;
+            if (UE8M0) {
+                const uint32_t bits = __float_as_uint(__fdiv_rn(amax, 448.0f));
+                const uint32_t ex = (bits >> 23) + ((bits & 0x7FFFFFu) ? 1u : 0u);
+                sc = __uint_as_float(ex >= 255u ? 0x7F800000u : ex << 23);
+                f = ex >= 255u ? 0.0f
+                               : __uint_as_float(ex == 254u ? 0x00400000u : (254u - ex) << 23);
+            } else {
+                // `448.0 / amax` in the published torch code is reciprocal-then-multiply
+                f = __fmul_rn(__frcp_rn(amax), 448.0f);
+                sc = __fdiv_rn(amax, 448.0f);
+            }
             uint32_t packed[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -94,7 +108,7 @@ __global__ void __launch_bounds__(kQuantThreads)
                 packed[0] = packed[1] = 0u;
             }
             *reinterpret_cast<uint2*>(qdst) = make_uint2(packed[0], packed[1]);
-            if (hl == 0) scale[(long long)r * nk + b] = src < 0 ? 0.0f : __fdiv_rn(amax, 448.0f);
+            if (hl == 0) scale[(long long)r * nk + b] = src < 0 ? 0.0f : sc;
         }
     }
 }
@@ -104,9 +118,9 @@ __global__ void __launch_bounds__(kQuantThreads)
 
 using namespace ferret;
 
-extern "C" int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows,
-                                          const int32_t* gather_rows, int gather_div, int R, int K,
-                                          void* a_fp8, float* a_scale, void* stream) {
+template <bool UE8M0>
+static int quant_act(const void* x_bf16, int x_rows, const int32_t* gather_rows, int gather_div,
+                     int R, int K, void* a_fp8, float* a_scale, void* stream) {
     if (R < 0 || K <= 0 || (K % 128) != 0 || x_rows < 0) return FERRET_ERR_SHAPE;
     if (!gather_rows && R > x_rows) return FERRET_ERR_SHAPE;
     if (R == 0) return FERRET_OK;
@@ -121,9 +135,22 @@ extern "C" int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows,
     const long long tasks = (long long)R * ((K / 128 + kBlocksPerTask - 1) / kBlocksPerTask);
     const long long want = (tasks + (kQuantThreads / 32) - 1) / (kQuantThreads / 32);
     const int grid = (int)(want < (long long)info->num_sms * 16 ? want : (long long)info->num_sms * 16);
-    return launch_kernel(quant_act_kernel, dim3(grid), dim3(kQuantThreads), 0, as_stream(stream),
-                         static_cast<const __nv_bfloat16*>(x_bf16), x_rows, gather_rows,
-                         gather_div, R, K, static_cast<uint8_t*>(a_fp8), a_scale, make_ctl(info));
+    return launch_kernel(quant_act_kernel<UE8M0>, dim3(grid), dim3(kQuantThreads), 0,
+                         as_stream(stream), static_cast<const __nv_bfloat16*>(x_bf16), x_rows,
+                         gather_rows, gather_div, R, K, static_cast<uint8_t*>(a_fp8), a_scale,
+                         make_ctl(info));
+}
+
+extern "C" int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows,
+                                          const int32_t* gather_rows, int gather_div, int R, int K,
+                                          void* a_fp8, float* a_scale, void* stream) {
+    return quant_act<false>(x_bf16, x_rows, gather_rows, gather_div, R, K, a_fp8, a_scale, stream);
+}
+
+extern "C" int ferret_quant_act_fp8_1x128_ue8m0(const void* x_bf16, int x_rows,
+                                                const int32_t* gather_rows, int gather_div, int R,
+                                                int K, void* a_fp8, float* a_scale, void* stream) {
+    return quant_act<true>(x_bf16, x_rows, gather_rows, gather_div, R, K, a_fp8, a_scale, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -96,18 +96,33 @@ def activations(T: int, K: int, seed: int = SEED_ACTS, device="cpu", scale: floa
     return (torch.randn(T, K, generator=g) * scale).to(torch.bfloat16).to(device)
 
 
-def per_block_cast_to_fp8(w: torch.Tensor):
-    """[..., N, K] float -> (e4m3 [..., N, K], f32 [..., N/128, K/128])."""
+def ceil_pow2(s: torch.Tensor) -> torch.Tensor:
+    """Smallest power of two >= s (positive normal float32), from the bits."""
+    bits = s.float().contiguous().view(torch.int32)
+    ex = (bits >> 23) + ((bits & 0x7FFFFF) != 0).to(torch.int32)
+    return (ex << 23).view(torch.float32)
+
+
+def per_block_cast_to_fp8(w: torch.Tensor, use_ue8m0: bool = False):
+    """[..., N, K] float -> (e4m3 [..., N, K], f32 [..., N/128, K/128]).
+
+    use_ue8m0 rounds each block scale up to a power of two (UE8M0) and divides
+    by it exactly -- the weights of the block-scaled GEMM path."""
     *lead, N, K = w.shape
     v = w.float().reshape(*lead, N // 128, 128, K // 128, 128)
     amax = v.abs().amax(dim=(-3, -1), keepdim=True).clamp(min=1e-4)
-    q = (v * (448.0 / amax)).to(torch.float8_e4m3fn).reshape(*lead, N, K)
-    s = (amax / 448.0).reshape(*lead, N // 128, K // 128)
+    if use_ue8m0:
+        sc = ceil_pow2(amax / 448.0)
+        q = (v * torch.reciprocal(sc)).to(torch.float8_e4m3fn).reshape(*lead, N, K)
+        s = sc.reshape(*lead, N // 128, K // 128)
+    else:
+        q = (v * (448.0 / amax)).to(torch.float8_e4m3fn).reshape(*lead, N, K)
+        s = (amax / 448.0).reshape(*lead, N // 128, K // 128)
     return q, s.contiguous()
 
 
 def fp8_weights(E: int, N: int, K: int, seed: int = SEED_WEIGHTS, device="cpu",
-                std: float = 0.02, chunk: int = 8):
+                std: float = 0.02, chunk: int = 8, use_ue8m0: bool = False):
     """Random-init FP8 expert weights, generated on `device` in expert chunks."""
     w_q = torch.empty(E, N, K, dtype=torch.float8_e4m3fn, device=device)
     w_s = torch.empty(E, N // 128, K // 128, dtype=torch.float32, device=device)
@@ -115,7 +130,7 @@ def fp8_weights(E: int, N: int, K: int, seed: int = SEED_WEIGHTS, device="cpu",
     for e0 in range(0, E, chunk):
         e1 = min(E, e0 + chunk)
         w = torch.randn(e1 - e0, N, K, generator=g, device=device) * std
-        q, s = per_block_cast_to_fp8(w)
+        q, s = per_block_cast_to_fp8(w, use_ue8m0)
         w_q[e0:e1] = q
         w_s[e0:e1] = s
         del w

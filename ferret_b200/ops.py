@@ -23,7 +23,7 @@ import ctypes
 
 import torch
 
-from ._lib import FERRET_SILU_MUL, FERRET_TILE_SHIFT, check, lib
+from ._lib import FERRET_SILU_MUL, FERRET_TILE_SHIFT, FERRET_UE8M0_SCALES, check, lib
 
 
 def _ptr(t: torch.Tensor | None):
@@ -99,9 +99,11 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
 
 
 def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = None,
-                          gather_div: int = 1, out=None):
+                          gather_div: int = 1, out=None, use_ue8m0: bool = False):
     """bf16 [rows, K] -> (e4m3 [R, K], f32 scales [R, K/128]).  With gather_rows,
-    output row r quantizes x[gather_rows[r] // gather_div] (negative -> zeros)."""
+    output row r quantizes x[gather_rows[r] // gather_div] (negative -> zeros).
+    use_ue8m0 rounds each scale up to a power of two (the input of the
+    block-scaled GEMM, ``disable_ue8m0_cast=False``)."""
     _need(x, torch.bfloat16, "x", 2)
     K = x.shape[1]
     R = x.shape[0] if gather_rows is None else gather_rows.shape[0]
@@ -112,9 +114,9 @@ def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = No
         s = torch.empty(R, K // 128, dtype=torch.float32, device=x.device)
     else:
         q, s = out
-    check(lib().ferret_quant_act_fp8_1x128(_ptr(x), x.shape[0], _ptr(gather_rows), gather_div, R,
-                                           K, _ptr(q), _ptr(s), _stream()),
-          "ferret_quant_act_fp8_1x128")
+    name = "ferret_quant_act_fp8_1x128_ue8m0" if use_ue8m0 else "ferret_quant_act_fp8_1x128"
+    check(getattr(lib(), name)(_ptr(x), x.shape[0], _ptr(gather_rows), gather_div, R, K, _ptr(q),
+                               _ptr(s), _stream()), name)
     return q, s
 
 
@@ -124,8 +126,12 @@ def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.T
                                      silu: bool = False, tile: int = 0) -> None:
     """out[r] = dequant(A[r]) @ dequant(W[m_indices[r]])^T with exact fp32 block scales.
 
-    ``disable_ue8m0_cast`` is accepted for signature compatibility; scales are
-    always applied in fp32 (never rounded to powers of two).
+    ``disable_ue8m0_cast=False`` declares every scale a power of two (UE8M0:
+    ``per_token_cast_to_fp8(..., use_ue8m0=True)`` activations and
+    ``data.per_block_cast_to_fp8(..., use_ue8m0=True)`` weights); 128-row
+    tiles then apply the scales inside the tensor-core MMA
+    (kind::mxf8f6f4.block_scale).  Other scales are never rounded: with the
+    default ``True`` they are applied in fp32 as given.
     """
     A, A_scale = a
     W, W_scale = b
@@ -152,7 +158,8 @@ def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.T
         ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=A.device)
     else:
         _need(expert_offsets, torch.int32, "expert_offsets", 1)
-    flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+    flags = ((FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+             | (0 if disable_ue8m0_cast else FERRET_UE8M0_SCALES))
     check(lib().ferret_fp8_grouped_gemm_nt_contiguous(
         _ptr(A), _ptr(A_scale), _ptr(W), _ptr(W_scale), _ptr(out), _ptr(m_indices),
         _ptr(expert_offsets), M, N, K, E, flags, _ptr(ws), ws_bytes, _stream()),
@@ -214,13 +221,16 @@ class W13Buffers:
 
 def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
                 W_scale: torch.Tensor, silu: bool = False, bufs: W13Buffers | None = None,
-                tile: int = 0):
+                tile: int = 0, use_ue8m0: bool = False):
     """The W13 hot path on one GPU.
 
     hidden bf16 [T, K], topk_ids int32 [T, topk], W e4m3 [E, N, K],
     W_scale f32 [E, N/128, K/128].  Returns (out, sorted_rows, expert_offsets):
     out bf16 [T*topk, N or N/2] in expert-sorted order; row i of out belongs to
     the (token, slot) pair sorted_rows[i] (= token*topk + slot).
+    use_ue8m0: W_scale holds powers of two (``per_block_cast_to_fp8(...,
+    use_ue8m0=True)``); activations get power-of-two scales too and the GEMM
+    applies both inside the MMA.
     """
     _need(hidden, torch.bfloat16, "hidden", 2)
     _need(topk_ids, torch.int32, "topk_ids", 2)
@@ -239,18 +249,19 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
                                _ptr(bufs.offsets), _ptr(bufs.m_indices), _ptr(bufs.perm_ws),
                                bufs.perm_ws_bytes, s),
           "ferret_moe_permute")
+    qname = "ferret_quant_act_fp8_1x128_ue8m0" if use_ue8m0 else "ferret_quant_act_fp8_1x128"
+    quant = getattr(L, qname)
     if bufs.quant_once:
         # each token once, then its topk routed copies in expert order
-        check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, None, 1, T, K, _ptr(bufs.q_tok),
-                                           _ptr(bufs.s_tok), s), "ferret_quant_act_fp8_1x128")
+        check(quant(_ptr(hidden), T, None, 1, T, K, _ptr(bufs.q_tok), _ptr(bufs.s_tok), s), qname)
         check(L.ferret_fp8_gather_rows(_ptr(bufs.q_tok), _ptr(bufs.s_tok), T,
                                        _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
                                        _ptr(bufs.a_scale), s), "ferret_fp8_gather_rows")
     else:
-        check(L.ferret_quant_act_fp8_1x128(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K,
-                                           _ptr(bufs.a), _ptr(bufs.a_scale), s),
-              "ferret_quant_act_fp8_1x128")
-    flags = (FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+        check(quant(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
+                    _ptr(bufs.a_scale), s), qname)
+    flags = ((FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
+             | (FERRET_UE8M0_SCALES if use_ue8m0 else 0))
     check(L.ferret_fp8_grouped_gemm_nt_contiguous(
         _ptr(bufs.a), _ptr(bufs.a_scale), _ptr(W), _ptr(W_scale), _ptr(bufs.out), None,
         _ptr(bufs.offsets), R, N, K, E, flags, None, 0, s), "ferret_fp8_grouped_gemm_nt_contiguous")

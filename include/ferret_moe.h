@@ -49,6 +49,11 @@ extern "C" {
 /* flags for the GEMM entry points */
 #define FERRET_SILU_MUL 0x1         /* fused SiLU(gate)*up epilogue, N_out = N/2 */
 #define FERRET_TILE_SHIFT 8         /* bits 8-15: force token tile (16,32,64,128); 0 = auto */
+#define FERRET_UE8M0_SCALES 0x2     /* every a_scale / w_scale is a power of two (UE8M0):
+                                       plain (no SiLU) 128-token-tile launches apply them inside
+                                       the tensor-core MMA (kind::mxf8f6f4.block_scale) from
+                                       their exponent bits; other launches keep the exact-scale
+                                       kernels (exact for such scales) */
 
 /* Library version (FERRET_MOE_VERSION). */
 FERRET_API int ferret_version(void);
@@ -136,6 +141,18 @@ FERRET_API int ferret_moe_align_block_size(const int32_t* topk_ids, int T, int t
 FERRET_API int ferret_quant_act_fp8_1x128(const void* x_bf16, int x_rows, const int32_t* gather_rows,
                                           int gather_div, int R, int K, void* a_fp8,
                                           float* a_scale, void* stream);
+
+/*
+ * The same quantizer with power-of-two (UE8M0) scales, the input of
+ * FERRET_UE8M0_SCALES.
+ * Replaces: DeepGEMM per_token_cast_to_fp8(x, use_ue8m0=True).
+ * Arguments and layouts as ferret_quant_act_fp8_1x128.  amax is clamped at
+ * 1e-4; scale = the smallest power of two >= fl(amax/448) (exact, from the
+ * fp32 bits); q = e4m3_satfinite(x * (1/scale)) (an exact product).
+ */
+FERRET_API int ferret_quant_act_fp8_1x128_ue8m0(const void* x_bf16, int x_rows,
+                                                const int32_t* gather_rows, int gather_div, int R,
+                                                int K, void* a_fp8, float* a_scale, void* stream);
 
 /*
  * Row gather of quantized rows (no reference counterpart; an alternative to

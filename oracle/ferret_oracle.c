@@ -16,7 +16,10 @@
  *   orc_quant_act_fp8_1x128            DeepGEMM per_token_cast_to_fp8 as
  *       called at baselines/fp8-group-gemm/baseline_dsv3_decode.py:42
  *       (use_ue8m0=False) with the layout of
- *       tasks/fp8-group-gemm-dsv3-decode.yaml:18-24.
+ *       tasks/fp8-group-gemm-dsv3-decode.yaml:18-24; orc_quant_act_fp8_1x128_ue8m0
+ *       the use_ue8m0=True form (power-of-two scales, the input of the
+ *       block-scaled UE8M0 MMA of
+ *       examples/fp8-group-gemm/v007_dsv3_decode_verified_105.cu:262).
  *   orc_fp8_grouped_gemm               the host reference cpu_ref_bs of
  *       examples/fp8-group-gemm/v007_dsv3_decode_verified_105.cu:441-467
  *       (same per-128-K-block fp32 dot, then sum += dot*sfa*sfb) but with
@@ -150,9 +153,8 @@ ORC_API void orc_moe_permute(const int32_t* topk_ids, int T, int topk, int E,
  * algorithm as torch executes it: amax clamped at 1e-4,
  * f = fl(fl(1/amax) * 448) (torch's `448.0 / t` is reciprocal-then-multiply),
  * q = e4m3_rne_satfinite(fl(x * f)), scale = fl(amax / 448). */
-ORC_API void orc_quant_act_fp8_1x128(const uint16_t* x, const int32_t* gather_rows,
-                                     int gather_div, int R, int K, uint8_t* q,
-                                     float* scale) {
+static void quant_act(const uint16_t* x, const int32_t* gather_rows, int gather_div, int R,
+                      int K, uint8_t* q, float* scale, int ue8m0) {
     int nk = K / 128;
     for (int r = 0; r < R; r++) {
         long src = r;
@@ -173,13 +175,43 @@ ORC_API void orc_quant_act_fp8_1x128(const uint16_t* x, const int32_t* gather_ro
                 if (v > amax) amax = v;
             }
             if (amax < 1e-4f) amax = 1e-4f;
-            /* torch evaluates `448.0 / amax` as reciprocal(amax) * 448 */
-            float f = (1.0f / amax) * 448.0f;
+            float f, sc;
+            if (ue8m0) {
+                /* smallest power of two >= fl(amax/448), from the fp32 bits */
+                float s0 = amax / 448.0f;
+                uint32_t bits, ex, sb, fb;
+                memcpy(&bits, &s0, 4);
+                ex = (bits >> 23) + ((bits & 0x7FFFFFu) ? 1u : 0u);
+                sb = ex >= 255u ? 0x7F800000u : ex << 23;
+                fb = ex >= 255u ? 0u : ex == 254u ? 0x00400000u : (254u - ex) << 23;
+                memcpy(&sc, &sb, 4);
+                memcpy(&f, &fb, 4);
+            } else {
+                /* torch evaluates `448.0 / amax` as reciprocal(amax) * 448 */
+                f = (1.0f / amax) * 448.0f;
+                sc = amax / 448.0f;
+            }
             for (int i = 0; i < 128; i++)
                 q[(long)r * K + b * 128 + i] = orc_f32_to_e4m3(orc_bf16_to_f32(xr[b * 128 + i]) * f);
-            scale[(long)r * nk + b] = amax / 448.0f;
+            scale[(long)r * nk + b] = sc;
         }
     }
+}
+
+ORC_API void orc_quant_act_fp8_1x128(const uint16_t* x, const int32_t* gather_rows,
+                                     int gather_div, int R, int K, uint8_t* q,
+                                     float* scale) {
+    quant_act(x, gather_rows, gather_div, R, K, q, scale, 0);
+}
+
+/* The use_ue8m0=True form of the same quantizer (DeepGEMM
+ * per_token_cast_to_fp8(x, use_ue8m0=True)): the scale is rounded up to a
+ * power of two -- here exactly, from the fp32 bits, rather than through a
+ * floating-point log2 -- and x is multiplied by its exact inverse. */
+ORC_API void orc_quant_act_fp8_1x128_ue8m0(const uint16_t* x, const int32_t* gather_rows,
+                                           int gather_div, int R, int K, uint8_t* q,
+                                           float* scale) {
+    quant_act(x, gather_rows, gather_div, R, K, q, scale, 1);
 }
 
 /* ------------------------------------------------------------------ */

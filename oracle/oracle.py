@@ -58,6 +58,7 @@ def lib():
         L.orc_f32_to_e4m3.restype = ctypes.c_uint8
         L.orc_moe_permute.argtypes = [_p, _i, _i, _i, _p, _p, _p]
         L.orc_quant_act_fp8_1x128.argtypes = [_p, _p, _i, _i, _i, _p, _p]
+        L.orc_quant_act_fp8_1x128_ue8m0.argtypes = [_p, _p, _i, _i, _i, _p, _p]
         L.orc_fp8_grouped_gemm.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]
         L.orc_int4_w13.argtypes = [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p]
     return _LIB
@@ -158,7 +159,7 @@ def moe_align_block_size(topk_ids: np.ndarray, E: int, block_size: int):
 
 
 def quant_act_fp8_1x128(x_bf16: np.ndarray, gather_rows: np.ndarray | None = None,
-                        gather_div: int = 1, R: int | None = None):
+                        gather_div: int = 1, R: int | None = None, ue8m0: bool = False):
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
     K = x.shape[1]
     if gather_rows is not None:
@@ -168,7 +169,8 @@ def quant_act_fp8_1x128(x_bf16: np.ndarray, gather_rows: np.ndarray | None = Non
         R = x.shape[0] if R is None else R
     q = np.empty((R, K), np.uint8)
     s = np.empty((R, K // 128), np.float32)
-    lib().orc_quant_act_fp8_1x128(_ptr(x), _ptr(gather_rows), gather_div, R, K, _ptr(q), _ptr(s))
+    fn = lib().orc_quant_act_fp8_1x128_ue8m0 if ue8m0 else lib().orc_quant_act_fp8_1x128
+    fn(_ptr(x), _ptr(gather_rows), gather_div, R, K, _ptr(q), _ptr(s))
     return q, s
 
 

@@ -89,6 +89,42 @@ def test_quant_oracle_matches_published_algorithm():
     assert np.array_equal(s.view(np.uint32), s_ref.numpy().view(np.uint32))
 
 
+def test_quant_ue8m0_oracle_matches_exact_restatement():
+    """use_ue8m0 form: scale = 2^ceil(log2(fl(amax/448))) evaluated exactly
+    (float64 log2 of a float32 is exact enough for the ceiling), q = the e4m3
+    of x / scale (exact)."""
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(64, 512, generator=g) * torch.logspace(-3, 3, 64).unsqueeze(1)).to(torch.bfloat16)
+    x[3] = 0                     # the 1e-4 clamp
+    x[5, :128] = 56.0            # amax / 448 = 1/8 exactly: kept, not rounded up
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    q, s = O.quant_act_fp8_1x128(xb, ue8m0=True)
+    xf = x.float().numpy().reshape(64, 4, 128).astype(np.float64)
+    amax = np.maximum(np.abs(xf).max(-1), 1e-4).astype(np.float32)
+    s_ref = np.exp2(np.ceil(np.log2((amax / np.float32(448)).astype(np.float64)))).astype(np.float32)
+    assert np.array_equal(s, s_ref)
+    assert s[5, 0] == 0.125
+    q_ref = torch.from_numpy((xf / s_ref[..., None]).astype(np.float32).reshape(64, 512))
+    assert np.array_equal(q, q_ref.to(torch.float8_e4m3fn).view(torch.uint8).numpy())
+    # the gathered form reads the same rows
+    rows = np.array([9, 0, -1, 4], np.int32)
+    qg, sg = O.quant_act_fp8_1x128(xb, rows, gather_div=3, ue8m0=True)
+    assert np.array_equal(qg[0], q[3]) and np.array_equal(sg[3], s[1])
+    assert not qg[2].any() and not sg[2].any()
+
+
+def test_ue8m0_weight_scales_are_powers_of_two():
+    from ferret_b200 import data
+    g = torch.Generator().manual_seed(8)
+    w = torch.randn(2, 256, 512, generator=g) * 0.02
+    q, s = data.per_block_cast_to_fp8(w, use_ue8m0=True)
+    assert (s.view(torch.int32) & 0x7FFFFF == 0).all()
+    q0, s0 = data.per_block_cast_to_fp8(w)
+    assert (s >= s0).all() and (s < 2 * s0).all()
+    deq = q.float().view(2, 2, 128, 4, 128) * s.view(2, 2, 1, 4, 1)
+    assert (deq.view(2, 256, 512) - w).abs().max() <= w.abs().max() / 8
+
+
 def test_quant_oracle_gather():
     g = torch.Generator().manual_seed(6)
     x = torch.randn(5, 256, generator=g).to(torch.bfloat16)
