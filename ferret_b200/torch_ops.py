@@ -6,11 +6,12 @@ this module gives the library the operator form, with the tensor signatures
 of the baselines it replaces:
 
 * ``ferret_moe::fp8_grouped_gemm_nt_contiguous(Tensor a, Tensor a_scale,
-  Tensor w, Tensor w_scale, Tensor(a!) out, Tensor m_indices, bool silu=False)
-  -> ()`` -- DeepGEMM's m_grouped_fp8_gemm_nt_contiguous
-  (baselines/fp8-group-gemm/baseline_dsv3_decode.py:55-57);
-* ``ferret_moe::per_token_cast_to_fp8(Tensor x) -> (Tensor, Tensor)``
-  (baseline_dsv3_decode.py:42);
+  Tensor w, Tensor w_scale, Tensor(a!) out, Tensor m_indices, bool silu=False,
+  bool disable_ue8m0_cast=True) -> ()`` -- DeepGEMM's
+  m_grouped_fp8_gemm_nt_contiguous (baselines/fp8-group-gemm/baseline_dsv3_decode.py:55-57;
+  ``disable_ue8m0_cast=False`` declares power-of-two scales);
+* ``ferret_moe::per_token_cast_to_fp8(Tensor x, bool use_ue8m0=False) ->
+  (Tensor, Tensor)`` (baseline_dsv3_decode.py:42);
 * ``ferret_moe::moe_align_block_size(Tensor topk_ids, int block_size,
   int num_experts) -> (Tensor, Tensor, Tensor)``
   (baselines/kimi-moe-w13-int4/baseline_marlin.py:123-126);
@@ -32,8 +33,8 @@ from . import ops
 
 _LIB = torch.library.Library("ferret_moe", "DEF")
 _LIB.define("fp8_grouped_gemm_nt_contiguous(Tensor a, Tensor a_scale, Tensor w, Tensor w_scale, "
-            "Tensor(a!) out, Tensor m_indices, bool silu=False) -> ()")
-_LIB.define("per_token_cast_to_fp8(Tensor x) -> (Tensor, Tensor)")
+            "Tensor(a!) out, Tensor m_indices, bool silu=False, bool disable_ue8m0_cast=True) -> ()")
+_LIB.define("per_token_cast_to_fp8(Tensor x, bool use_ue8m0=False) -> (Tensor, Tensor)")
 _LIB.define("moe_align_block_size(Tensor topk_ids, int block_size, int num_experts) "
             "-> (Tensor, Tensor, Tensor)")
 _LIB.define("int4_moe_w13(Tensor hidden, Tensor w_raw, Tensor w_scale, Tensor topk_ids, "
@@ -44,12 +45,13 @@ _LIB.define("int4_moe_w13(Tensor hidden, Tensor w_raw, Tensor w_scale, Tensor to
 _INT4_CACHE: list = []
 
 
-def _fp8_gemm(a, a_scale, w, w_scale, out, m_indices, silu=False):
-    ops.m_grouped_fp8_gemm_nt_contiguous((a, a_scale), (w, w_scale), out, m_indices, silu=silu)
+def _fp8_gemm(a, a_scale, w, w_scale, out, m_indices, silu=False, disable_ue8m0_cast=True):
+    ops.m_grouped_fp8_gemm_nt_contiguous((a, a_scale), (w, w_scale), out, m_indices,
+                                         disable_ue8m0_cast=disable_ue8m0_cast, silu=silu)
 
 
-def _quant(x):
-    return ops.per_token_cast_to_fp8(x)
+def _quant(x, use_ue8m0=False):
+    return ops.per_token_cast_to_fp8(x, use_ue8m0=use_ue8m0)
 
 
 def _align(topk_ids, block_size, num_experts):

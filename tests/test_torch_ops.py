@@ -10,6 +10,8 @@ import ferret_b200.torch_ops  # noqa: F401  (registers torch.ops.ferret_moe)
 def test_schemas_registered():
     s = str(torch.ops.ferret_moe.fp8_grouped_gemm_nt_contiguous.default._schema)
     assert "Tensor(a!) out" in s and "Tensor m_indices" in s and "bool silu=False" in s
+    assert "bool disable_ue8m0_cast=True" in s
+    assert "bool use_ue8m0=False" in str(torch.ops.ferret_moe.per_token_cast_to_fp8.default._schema)
     for name in ("per_token_cast_to_fp8", "moe_align_block_size", "int4_moe_w13"):
         assert hasattr(torch.ops.ferret_moe, name)
 
@@ -33,6 +35,9 @@ def test_ops_match_python_api(cuda_device):
     ops.m_grouped_fp8_gemm_nt_contiguous((a, a_s), (W, Ws), out2, mi)
     torch.cuda.synchronize()
     assert torch.equal(out1.view(torch.int16), out2.view(torch.int16))
+    qu, su = torch.ops.ferret_moe.per_token_cast_to_fp8(hidden, True)
+    qv, sv = ops.per_token_cast_to_fp8(hidden, use_ue8m0=True)
+    assert torch.equal(qu.view(torch.uint8), qv.view(torch.uint8)) and torch.equal(su, sv)
     si, ei, ni = torch.ops.ferret_moe.moe_align_block_size(ids, 16, E)
     sj, ej, nj = ops.moe_align_block_size(ids, 16, E)
     assert torch.equal(si, sj) and torch.equal(ei, ej) and torch.equal(ni, nj)
