@@ -89,6 +89,11 @@ def test_permute_and_quant_validation(L):
     assert q(P, 2, None, 1, 4, 128, P, P, None) == -1      # R > x_rows without gather
     assert q(P, 4, None, 1, 0, 128, P, P, None) == 0
     assert q(None, 4, None, 1, 4, 128, P, P, None) == -3
+    u = L.ferret_quant_act_fp8_1x128_ue8m0          # same validation in the UE8M0 form
+    assert u(P, 4, None, 1, 4, 100, P, P, None) == -1
+    assert u(P, 4, P, 0, 4, 128, P, P, None) == -1
+    assert u(P, 4, None, 1, 0, 128, P, P, None) == 0
+    assert u(None, 4, None, 1, 4, 128, P, P, None) == -3
 
 
 def test_status_requires_pointer(L):

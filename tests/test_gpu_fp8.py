@@ -102,7 +102,7 @@ def test_permute_chunked_matches_single_cta(ops, T, topk, E, lo, hi):
 
 # ---------------------------------------------------------------- quantization
 
-@pytest.mark.parametrize("R,K", [(1, 128), (37, 512), (1024, 7168)])
+@pytest.mark.parametrize("R,K", [(1, 128), (37, 512), (1024, 7168), (3, 16384)])
 def test_quant_bit_exact(ops, R, K):
     g = torch.Generator().manual_seed(R)
     x = (torch.randn(R, K, generator=g) * torch.logspace(-5, 2, R).unsqueeze(1)).to(torch.bfloat16)
@@ -244,6 +244,9 @@ CASES = [
     ([32], 1024, 2048, 0, False, 0),
     ([32], 1024, 2048, 0, True, 0),
     ([3, 0, 9], 512, 7168, 0, True, 16),
+    # the K limit (K = 16384: 128 K blocks) on the swap-AB and the prefill kernel
+    ([3] * 16, 256, 16384, 0, False, 0),
+    ([130, 3], 256, 16384, 0, True, 128),
 ]
 
 

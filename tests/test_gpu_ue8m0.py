@@ -78,6 +78,7 @@ CASES = [
     ([200, 300], 512, 7168, 0, False),              # 56 K blocks: the scale ring wraps 7 times
     ([200, 300], 512, 7168, 0, True),
     ([1500] * 4, 1024, 1024, 0, False),             # 192 tiles: CTAs reuse the accumulator
+    ([130, 3], 256, 16384, 0, False),               # the K limit: 128 K blocks
 ]
 
 
