@@ -158,6 +158,33 @@ def moe_align_block_size(topk_ids: np.ndarray, E: int, block_size: int):
     return sorted_ids, expert_ids, np.array([p], np.int32)
 
 
+def per_block_cast_to_fp8(w: np.ndarray, ue8m0: bool = False):
+    """128x128 block weight quantization: DeepGEMM per_block_cast_to_fp8 as
+    called at baselines/fp8-group-gemm/baseline_dsv3_decode.py:44-47
+    (use_ue8m0=False), restated with IEEE float32 steps.
+
+    w: float32 [..., N, K], N and K multiples of 128.  Per block: amax =
+    max|w| clamped at 1e-4; f = fl(fl(1/amax) * 448) (torch's `448.0 / amax`
+    is reciprocal-then-multiply); q = e4m3_rne_satfinite(fl(w * f)); scale =
+    fl(amax / 448).  ue8m0: scale = the smallest power of two >= fl(amax /
+    448) (from the bits) and f = its exact inverse.
+    Returns (e4m3 bytes [..., N, K], float32 scales [..., N/128, K/128])."""
+    w = np.ascontiguousarray(w, np.float32)
+    *lead, N, K = w.shape
+    v = w.reshape(*lead, N // 128, 128, K // 128, 128)
+    amax = np.maximum(np.abs(v).max(axis=(-3, -1), keepdims=True), np.float32(1e-4))
+    s = (amax / np.float32(448)).astype(np.float32)
+    if ue8m0:
+        bits = s.view(np.uint32)
+        ex = (bits >> 23) + ((bits & 0x7FFFFF) != 0).astype(np.uint32)
+        s = (ex << 23).astype(np.uint32).view(np.float32)
+        f = ((254 - ex) << 23).astype(np.uint32).view(np.float32)
+    else:
+        f = ((np.float32(1) / amax).astype(np.float32) * np.float32(448)).astype(np.float32)
+    q = f32_to_e4m3((v * f).astype(np.float32)).reshape(*lead, N, K)
+    return q, np.ascontiguousarray(s.reshape(*lead, N // 128, K // 128))
+
+
 def quant_act_fp8_1x128(x_bf16: np.ndarray, gather_rows: np.ndarray | None = None,
                         gather_div: int = 1, R: int | None = None, ue8m0: bool = False):
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)

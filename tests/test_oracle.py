@@ -113,6 +113,22 @@ def test_quant_ue8m0_oracle_matches_exact_restatement():
     assert not qg[2].any() and not sg[2].any()
 
 
+@pytest.mark.parametrize("ue8m0", [False, True])
+def test_weight_block_quant_matches_oracle(ue8m0):
+    """The load-time weight quantizer (torch) against the oracle's restatement
+    of the published per_block_cast_to_fp8, bit for bit: zero blocks (the 1e-4
+    clamp), an outlier block and magnitudes over 8 decades."""
+    from ferret_b200 import data
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(3, 384, 512, generator=g) * torch.logspace(-4, 4, 3 * 384).view(3, 384, 1)
+    w[0, :128, :128] = 0
+    w[1, 200, 300] = 1e5
+    q, s = data.per_block_cast_to_fp8(w, use_ue8m0=ue8m0)
+    qr, sr = O.per_block_cast_to_fp8(w.numpy(), ue8m0=ue8m0)
+    assert np.array_equal(q.view(torch.uint8).numpy(), qr)
+    assert np.array_equal(s.numpy().view(np.uint32), sr.view(np.uint32))
+
+
 def test_ue8m0_weight_scales_are_powers_of_two():
     from ferret_b200 import data
     g = torch.Generator().manual_seed(8)
