@@ -56,6 +56,9 @@ def parse_args():
                     help="FP8 block scales: fp32 (exact, the reference contract) or ue8m0 "
                          "(power-of-two weights and activations; the 128-row-tile GEMM applies "
                          "them inside the MMA, kind::mxf8f6f4.block_scale)")
+    ap.add_argument("--prefill-pairs", action="store_true",
+                    help="128-token-tile launches put each expert's whole 256-row chunks on CTA "
+                         "pairs (tcgen05.mma.cta_group::2)")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="profiling aid: run N bare GEMM launches and exit")
     return ap.parse_args()
@@ -277,6 +280,7 @@ def run_single(args, cfg):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ue8m0 = getattr(args, "scales", "fp32") == "ue8m0"
+    pairs = bool(getattr(args, "prefill_pairs", False))
     W, W_s = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev, use_ue8m0=ue8m0)
     hidden = data.activations(cfg.T, cfg.K).to(dev)
     ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s).to(dev)
@@ -284,12 +288,14 @@ def run_single(args, cfg):
     bufs = ops.W13Buffers(cfg.T, cfg.topk, cfg.K, n_out, cfg.E, dev)
 
     def step():
-        ops.fp8_moe_w13(hidden, ids, W, W_s, silu=cfg.silu, bufs=bufs, use_ue8m0=ue8m0)
+        ops.fp8_moe_w13(hidden, ids, W, W_s, silu=cfg.silu, bufs=bufs, use_ue8m0=ue8m0,
+                        prefill_pairs=pairs)
 
     def gemm():
         ops.m_grouped_fp8_gemm_nt_contiguous((bufs.a, bufs.a_scale), (W, W_s), bufs.out, None,
                                              disable_ue8m0_cast=not ue8m0,
-                                             expert_offsets=bufs.offsets, silu=cfg.silu)
+                                             expert_offsets=bufs.offsets, silu=cfg.silu,
+                                             prefill_pairs=pairs)
 
     if args.gemm_only:
         step()
@@ -340,7 +346,7 @@ def run_single(args, cfg):
         d_hidden.copy_(h_hidden, non_blocking=True)
         d_ids.copy_(h_ids, non_blocking=True)
         out, _, _ = ops.fp8_moe_w13(d_hidden, d_ids, W, W_s, silu=cfg.silu, bufs=bufs,
-                                    use_ue8m0=ue8m0)
+                                    use_ue8m0=ue8m0, prefill_pairs=pairs)
         h_out.copy_(out, non_blocking=True)
     e2e()
     e2e_ms = timed(e2e, args.steps)
@@ -357,7 +363,8 @@ def run_single(args, cfg):
     pk = peaks()
     # the library runs the prefill kernel when experts average more than 48 rows
     prefill = (cfg.R + cfg.E - 1) // cfg.E > 48 and cfg.N % 256 == 0
-    kname = (("fp8_w13_prefill_mx_kernel" if ue8m0 else "fp8_w13_prefill_kernel") if prefill
+    kname = (("fp8_w13_prefill_mx_kernel" if ue8m0 and not cfg.silu
+              else "fp8_w13_prefill_pair_kernel" if pairs else "fp8_w13_prefill_kernel") if prefill
              else "fp8_w13_grouped_kernel")
     rl = roofline(byts, flops, g_ms, pk, kname)
     res = {
@@ -377,6 +384,7 @@ def run_single(args, cfg):
                    "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
                    "scales": "ue8m0 (powers of two)" if ue8m0 else "fp32 (exact)",
+                   "prefill_pairs": pairs,
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "hbm_gbs_step": round(byts / (ms * 1e-3) / 1e9, 1),
         "roofline": dict(rl, traffic=read_traffic(f"{rl['kernel'].removesuffix('_kernel')}_{cfg.name}")),
@@ -385,8 +393,8 @@ def run_single(args, cfg):
                 "h2d_bytes_per_step": h_hidden.numel() * 2 + h_ids.numel() * 4,
                 "d2h_bytes_per_step": h_out.numel() * 2},
         # permute (1, or count/scan/scatter), quant (1, or quant-once + gather), GEMM
-        "gpu_launches": ((3 if bufs.perm_ws_bytes else 1) + (2 if bufs.quant_once else 1) + 1)
-                        * args.steps,
+        "gpu_launches": ((3 if bufs.perm_ws_bytes else 1) + (2 if bufs.quant_once else 1)
+                         + (2 if pairs and prefill else 1)) * args.steps,
         "clocks": clk,
         "output_finite": out_ok,
     }
@@ -481,6 +489,7 @@ def run_single_int4(args, cfg):
                    "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
                    "scales": "ue8m0 (powers of two)" if ue8m0 else "fp32 (exact)",
+                   "prefill_pairs": pairs,
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "int4_weight_tbs": round(wbytes / (g_ms * 1e-3) / 1e12, 3),
         "roofline": {"bound": "hbm", "kernel": "int4_w13_grouped_kernel",

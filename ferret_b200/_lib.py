@@ -18,6 +18,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "ferret_moe.h")
 FERRET_SILU_MUL = 0x1
 FERRET_TILE_SHIFT = 8
 FERRET_UE8M0_SCALES = 0x2
+FERRET_PREFILL_PAIRS = 0x4
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

@@ -93,6 +93,55 @@ inline int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t s
     return FERRET_OK;
 }
 
+// The same for a kernel of CTA pairs (thread-block clusters of 2 along x).
+// grid.x must be even.
+template <typename... KArgs, typename... Args>
+inline int launch_kernel_pairs(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    return FERRET_OK;
+}
+
+// How many CTA pairs of `kern` (block threads, smem bytes) can be resident at
+// once; 0 if the query fails.
+template <typename... KArgs>
+inline int max_resident_pairs(void (*kern)(KArgs...), dim3 block, size_t smem) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
 // Maps a launch error to FERRET_ERR_CUDA (and clears it).
 inline int launch_status() {
     cudaError_t e = cudaGetLastError();

@@ -255,6 +255,113 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, ui
         : "memory");
 }
 
+// ------------------------------------------------- CTA pairs (cta_group::2)
+// A pair is a thread-block cluster of 2; the even CTA (rank 0) leads: it
+// issues the pair's MMAs, which read A and B from both CTAs' shared memory at
+// the same offsets and write each CTA's own Tensor Memory.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes, wait for the peer.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+// Shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of either CTA of the cluster (release, cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
+                 : "memory");
+}
+
+// try_wait with acquire at cluster scope (the barrier receives arrivals from
+// the peer CTA), with the suspend-time hint.
+__device__ __forceinline__ bool mbar_test_cl(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+// Pair MMA: D (each CTA: its 128 rows x N) (+)= A (128 rows per CTA) * B^T (N/2
+// rows per CTA), e4m3 operands, fp32 accumulate.  Leader CTA only.
+__device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "setp.ne.b32 P, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, P;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the mbarrier at shared::cluster address `cl_bar` (either CTA)
+// when the pair MMAs this thread issued so far are done.
+__device__ __forceinline__ void tc_commit_pair(uint32_t cl_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     cl_bar)
+                 : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion (bytes) is
+// counted on the mbarrier at shared::cluster address `cl_bar`, which may be
+// the leader CTA's.  Same x alignment rule as tma_load_2d.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int x, int y,
+                                                 uint32_t cl_bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(cl_bar), "l"(policy)
+        : "memory");
+}
+
+// mbar_wait for barriers that receive arrivals from the peer CTA of a pair.
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             const DevCtl& ctl, int site, bool respect_abort = true) {
+    if (mbar_test_cl(bar, parity, 0u)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_test_cl(bar, parity, 500000u)) return true;
+        if (respect_abort && *abort_flag) return false;
+        if (global_ns() - t0 > ctl.timeout_ns) {
+            *abort_flag = 1;
+            report(ctl, DEV_TIMEOUT | (site << 8));
+            return false;
+        }
+    }
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, f16/bf16 operands, fp32 accumulate.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {

@@ -611,7 +611,9 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
     return L;
 }
 
-template <bool PAIR>
+// REM: only the rows of each expert past its whole 256-row chunks (which the
+// CTA-pair kernel below takes), i.e. its last count % 256 rows.
+template <bool PAIR, bool REM = false>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
@@ -670,6 +672,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             seg_bad = true;
             s = min(max(s, 0), M);
             c = min(max(c, 0), M - s);
+        }
+        if (REM) {
+            s += c & ~255;
+            c &= 255;
         }
         seg_s[e] = s;
         seg_c[e] = c;
@@ -1463,6 +1469,372 @@ int launch_fp8_prefill_mx(const DeviceInfo* info, const void* a, const float* a_
     return launch_kernel(kern, dim3(info->num_sms), dim3(kMxThreads), smem, stream, tm_w, tm_a, g);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair form of the prefill kernel (FERRET_PREFILL_PAIRS) for each expert's
+// whole 256-row chunks; the rows past them go to fp8_w13_prefill_kernel<.., true>.
+//
+// A pair (thread-block cluster of 2) computes a 256-token x 256-weight-row
+// tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32): CTA r holds
+// token rows [128r, 128r+128) of the tile and weight rows [128r, 128r+128)
+// (gate block for r = 0 and up block for r = 1 with SiLU), and receives the
+// 128 x 256 partial of its own token rows in its own Tensor Memory.  Per SM
+// that is 32 KB of operands per K block instead of 48 KB for the same MMA
+// work, so the L2->SM stream shrinks by a third and 6 stages fit.
+//
+// Protocol (no multicast loads anywhere):
+//   * both CTAs load their halves with .cta_group::2 TMA, completing on the
+//     leader's (rank 0) full barrier, which the leader arms with both halves'
+//     bytes;
+//   * the leader's single MMA thread waits for it, issues the pair MMAs and
+//     commits to each CTA's empty barrier (stage free) and tfull barrier
+//     (K-block partial ready);
+//   * each CTA's 8 epilogue warps promote their own partial exactly as the
+//     single-CTA kernel does and release the buffer with one arrive per warp
+//     on the leader's tempty barrier (16 arrivals);
+//   * a cluster barrier after the roles finish keeps either CTA from leaving
+//     while the other still reads its shared memory or Tensor Memory.
+//
+// Measured on B200 (benchmark configuration 3, GEMM alone): 4.311 ms for this
+// kernel plus the single-CTA remainder launch, against 2.708 ms for the
+// single-CTA kernel alone.  With exact fp32 scales every K block's partial has
+// to be promoted by both CTAs before the leader can reuse one of the two TMEM
+// buffers, which puts a cross-SM round trip (tfull to the peer, the peer's
+// promotion, its arrive back on the leader) on every K block.  Hence opt-in;
+// the pair protocol itself is the base for the block-scaled pair tile, whose
+// single accumulator needs one such handshake per tile.
+// ---------------------------------------------------------------------------
+constexpr int kPpStage = 128 * 128 + 128 * 128;    // A half 16 KB + B half 16 KB
+constexpr int kPpMaxStages = 6;
+
+enum : int { SITE_PEER_EMPTY = 9, SITE_PEER_TAIL = 10 };
+
+struct PpLayout {
+    int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
+};
+
+__host__ __device__ inline PpLayout pp_layout(int stages, int E) {
+    PpLayout L;
+    int o = 0;
+    L.stages_off = o;
+    o += kPpStage * stages;
+    L.segs_off = o;
+    o += 4 * E;
+    L.segc_off = o;
+    o += 4 * E;
+    L.mts_off = o;
+    o += 4 * (E + 1);
+    L.part_off = o;
+    o += 4 * (kPfThreads + 1);
+    o = (o + 7) & ~7;
+    L.bar_off = o;
+    o += 8 * (2 * kPpMaxStages + 2 * 2 + 1);
+    L.misc_off = o;
+    o += 16;
+    L.total = o;
+    return L;
+}
+
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const PpLayout L = pp_layout(NS, E);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPpMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPpMaxStages + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);            // the leader's arm; bytes from both CTAs
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * (kPfEpi / 32));   // one per epilogue warp of both CTAs
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), 512);
+        tmem_relinquish_pair();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        seg_s[e] = s;
+        seg_c[e] = c & ~255;                      // whole 256-row chunks only
+        mt_start[e] = c >> 8;
+    }
+    if (seg_bad && leader) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                               // both CTAs' barriers are initialised
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer (both CTAs) =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                int e, row0, rows, nb;
+                decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int arow = row0 + 128 * (int)rank;
+                const int wrow = PAIR ? e * N + (rank ? (N >> 1) : 0) + nb * 128
+                                      : e * N + nb * 256 + 128 * (int)rank;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait_cl(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl,
+                                      SITE_PEER_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(full_bar(s), 2 * kPpStage);
+                    const uint32_t dst = stage_base + s * kPpStage;
+                    const uint32_t bar = mapa_shared(full_bar(s), 0);
+                    tma_load_2d_pair(dst, &tm_a, kb * 128, arow, bar, pol);
+                    tma_load_2d_pair(dst + 16384, &tm_w, kb * 128, wrow, bar, pol);
+                }
+            }
+            // the last stages are free again once the leader's MMAs consumed
+            // them, which also means this CTA's loads into them have landed
+            for (int i = max(0, it - NS); i < it; ++i)
+                if (!mbar_wait_cl(empty_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl,
+                                  SITE_PEER_TAIL, false))
+                    break;
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer (leader CTA) =================
+        if (leader && elect_one()) {
+            constexpr uint32_t idesc = make_idesc(256, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait_cl(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl,
+                                      SITE_TEMPTY) ||
+                        !mbar_wait_cl(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPpStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4_pair(d, sdesc_k_sw128(st + ks * 32),
+                                        sdesc_k_sw128(st + 16384 + ks * 32), idesc, ks > 0);
+                    tc_commit_pair(empty_bar(s));
+                    tc_commit_pair(mapa_shared(empty_bar(s), 1));
+                    tc_commit_pair(tfull_bar(a));
+                    tc_commit_pair(mapa_shared(tfull_bar(a), 1));
+                }
+            }
+            tc_commit_pair(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else {
+        // ================= epilogue: promotion + store (both CTAs) =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = this CTA's rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        RingPos ra;
+        for (int t = pair; t < total; t += npairs) {
+            int e, row0, rows, nb;
+            decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const int my0 = row0 + 128 * (int)rank;
+            const bool live = 128 * (int)rank + r < rows;
+            const float* as_row = args.a_scale + (size_t)(my0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait_cl(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                          args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(ra.slot), 0));
+            }
+            if (!ok) break;
+            int orow = my0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + my0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            if (live && orow >= 0) {
+                __nv_bfloat16* o = args.out + (size_t)orow * ldo;
+                if (PAIR) {
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 pk;
+                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                        }
+                        dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                               // the pair's MMAs and arrivals are done
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc_pair(tmem_base, 512);
+    }
+}
+
+template <bool PAIR>
+int launch_fp8_prefill_pairs(const DeviceInfo* info, const void* a, const float* a_scale,
+                             const void* w, const float* w_scale, void* out, const int32_t* seg,
+                             int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
+                             const OutMap& om) {
+    CUtensorMap tm_w, tm_a;
+    int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
+                          128, true);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
+    if (rc != FERRET_OK) return rc;
+    const int budget = info->max_smem_optin - 1024;
+    const int stages = std::min(kPpMaxStages, (budget - pp_layout(0, E).total) / kPpStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const int smem = pp_layout(stages, E).total + 1024;
+    auto kern = fp8_w13_prefill_pair_kernel<PAIR>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    const int pairs = std::min(max_resident_pairs(kern, dim3(kPfThreads), smem), info->num_sms / 2);
+    if (pairs < 1) return FERRET_ERR_UNSUPPORTED;
+    GemmArgs g;
+    g.a_scale = a_scale;
+    g.w_scale = w_scale;
+    g.seg = seg;
+    g.seg_pairs = seg_pairs;
+    g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_rows = om.rows;
+    g.out_total = om.total;
+    g.out_peers = nullptr;
+    g.peer_rows = 0;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.E = E;
+    g.stages = stages;
+    g.ctl = make_ctl(info);
+    rc = launch_kernel_pairs(kern, dim3(2 * pairs), dim3(kPfThreads), smem, stream, tm_w, tm_a, g);
+    if (rc != FERRET_OK) return rc;
+    // the rows past each expert's whole 256-row chunks
+    const int stages1 = std::min(kPfMaxStages, (budget - pf_layout(0, E, false).total) / kPfStage);
+    if (stages1 < 2) return FERRET_ERR_SHAPE;
+    const int smem1 = pf_layout(stages1, E, false).total + 1024;
+    auto kern1 = fp8_w13_prefill_kernel<PAIR, true>;
+    if (cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    g.stages = stages1;
+    return launch_kernel(kern1, dim3(info->num_sms), dim3(kPfThreads), smem1, stream, tm_w, tm_a, g);
+}
+
 template <bool PAIR, bool STAGED>
 int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
                        const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
@@ -1544,6 +1916,12 @@ int run_fp8_gemm(const DeviceInfo* info, const void* a, const float* a_scale, co
     if (use_prefill(rows_hint, E, flags, N) && (flags & FERRET_UE8M0_SCALES) && !pair && !om.peers)
         return launch_fp8_prefill_mx(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M, N, K, E,
                                      s, om);
+    // CTA pairs for whole 256-row expert chunks, single CTAs for the rest
+    if (use_prefill(rows_hint, E, flags, N) && (flags & FERRET_PREFILL_PAIRS) && !om.peers)
+        return pair ? launch_fp8_prefill_pairs<true>(info, a, a_scale, w, w_scale, out, seg,
+                                                     seg_pairs, M, N, K, E, s, om)
+                    : launch_fp8_prefill_pairs<false>(info, a, a_scale, w, w_scale, out, seg,
+                                                      seg_pairs, M, N, K, E, s, om);
     if (use_prefill(rows_hint, E, flags, N))
         return pair ? launch_fp8_prefill<true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
                                                N, K, E, s, om)

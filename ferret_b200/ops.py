@@ -23,7 +23,8 @@ import ctypes
 
 import torch
 
-from ._lib import FERRET_SILU_MUL, FERRET_TILE_SHIFT, FERRET_UE8M0_SCALES, check, lib
+from ._lib import (FERRET_PREFILL_PAIRS, FERRET_SILU_MUL, FERRET_TILE_SHIFT, FERRET_UE8M0_SCALES,
+                   check, lib)
 
 
 def _ptr(t: torch.Tensor | None):
@@ -123,7 +124,8 @@ def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = No
 def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.Tensor | None,
                                      disable_ue8m0_cast: bool = True,
                                      expert_offsets: torch.Tensor | None = None,
-                                     silu: bool = False, tile: int = 0) -> None:
+                                     silu: bool = False, tile: int = 0,
+                                     prefill_pairs: bool = False) -> None:
     """out[r] = dequant(A[r]) @ dequant(W[m_indices[r]])^T with exact fp32 block scales.
 
     ``disable_ue8m0_cast=False`` declares every scale a power of two (UE8M0:
@@ -131,7 +133,8 @@ def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.T
     ``data.per_block_cast_to_fp8(..., use_ue8m0=True)`` weights); 128-row
     tiles then apply the scales inside the tensor-core MMA
     (kind::mxf8f6f4.block_scale).  Other scales are never rounded: with the
-    default ``True`` they are applied in fp32 as given.
+    default ``True`` they are applied in fp32 as given.  ``prefill_pairs`` runs
+    each expert's whole 256-row chunks on CTA pairs (tcgen05.mma.cta_group::2).
     """
     A, A_scale = a
     W, W_scale = b
@@ -159,7 +162,8 @@ def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.T
     else:
         _need(expert_offsets, torch.int32, "expert_offsets", 1)
     flags = ((FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
-             | (0 if disable_ue8m0_cast else FERRET_UE8M0_SCALES))
+             | (0 if disable_ue8m0_cast else FERRET_UE8M0_SCALES)
+             | (FERRET_PREFILL_PAIRS if prefill_pairs else 0))
     check(lib().ferret_fp8_grouped_gemm_nt_contiguous(
         _ptr(A), _ptr(A_scale), _ptr(W), _ptr(W_scale), _ptr(out), _ptr(m_indices),
         _ptr(expert_offsets), M, N, K, E, flags, _ptr(ws), ws_bytes, _stream()),
@@ -221,7 +225,7 @@ class W13Buffers:
 
 def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
                 W_scale: torch.Tensor, silu: bool = False, bufs: W13Buffers | None = None,
-                tile: int = 0, use_ue8m0: bool = False):
+                tile: int = 0, use_ue8m0: bool = False, prefill_pairs: bool = False):
     """The W13 hot path on one GPU.
 
     hidden bf16 [T, K], topk_ids int32 [T, topk], W e4m3 [E, N, K],
@@ -230,7 +234,8 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
     the (token, slot) pair sorted_rows[i] (= token*topk + slot).
     use_ue8m0: W_scale holds powers of two (``per_block_cast_to_fp8(...,
     use_ue8m0=True)``); activations get power-of-two scales too and the GEMM
-    applies both inside the MMA.
+    applies both inside the MMA.  prefill_pairs: CTA-pair tiles for whole
+    256-row expert chunks.
     """
     _need(hidden, torch.bfloat16, "hidden", 2)
     _need(topk_ids, torch.int32, "topk_ids", 2)
@@ -261,7 +266,8 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
         check(quant(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
                     _ptr(bufs.a_scale), s), qname)
     flags = ((FERRET_SILU_MUL if silu else 0) | (tile << FERRET_TILE_SHIFT)
-             | (FERRET_UE8M0_SCALES if use_ue8m0 else 0))
+             | (FERRET_UE8M0_SCALES if use_ue8m0 else 0)
+             | (FERRET_PREFILL_PAIRS if prefill_pairs else 0))
     check(L.ferret_fp8_grouped_gemm_nt_contiguous(
         _ptr(bufs.a), _ptr(bufs.a_scale), _ptr(W), _ptr(W_scale), _ptr(bufs.out), None,
         _ptr(bufs.offsets), R, N, K, E, flags, None, 0, s), "ferret_fp8_grouped_gemm_nt_contiguous")

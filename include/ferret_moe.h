@@ -54,6 +54,10 @@ extern "C" {
                                        the tensor-core MMA (kind::mxf8f6f4.block_scale) from
                                        their exponent bits; other launches keep the exact-scale
                                        kernels (exact for such scales) */
+#define FERRET_PREFILL_PAIRS 0x4    /* 128-token-tile launches: each expert's whole 256-row chunks
+                                       on CTA pairs (tcgen05.mma.cta_group::2, 256x256 tiles),
+                                       the rest on single CTAs; same results, measured slower with
+                                       exact scales (a cross-SM handshake per K block) */
 
 /* Library version (FERRET_MOE_VERSION). */
 FERRET_API int ferret_version(void);

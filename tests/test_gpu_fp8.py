@@ -261,6 +261,45 @@ def test_grouped_gemm_vs_oracle(ops, seg, N, K, pad, silu, tile, use_offsets):
     check(out, ref, mi)
 
 
+PAIR_CASES = [
+    # (seg_counts, N, K, silu): whole 256-row chunks on CTA pairs, the rest on single CTAs
+    ([600, 0, 256, 255, 1000, 3], 512, 512, False),
+    ([600, 0, 256, 255, 1000, 3], 512, 512, True),
+    ([1024], 256, 7168, False),
+    ([513, 770], 1024, 384, True),
+    ([100, 37], 256, 256, False),                   # no whole chunk: the single-CTA part only
+]
+
+
+@pytest.mark.parametrize("seg,N,K,silu", PAIR_CASES)
+@pytest.mark.parametrize("use_offsets", [False, True])
+def test_grouped_gemm_cta_pairs_vs_oracle(ops, seg, N, K, silu, use_offsets):
+    """FERRET_PREFILL_PAIRS: tcgen05.mma.cta_group::2 tiles for each expert's
+    whole 256-row chunks against the oracle, and equal to the single-CTA
+    prefill kernel (same per-K-block promotion order)."""
+    a, a_s, w, w_s, mi = make_case(hash((tuple(seg), N, K, 2)) & 0xFFFF, seg, N, K)
+    M = len(mi)
+    outs = []
+    for pairs in (True, False):
+        out = torch.full((M, N // 2 if silu else N), BF16_NAN, dtype=torch.int16).view(torch.bfloat16).cuda()
+        offs = None
+        if use_offsets:
+            offs = torch.from_numpy(np.concatenate([[0], np.cumsum(np.bincount(mi, minlength=len(seg)))])
+                                    .astype(np.int32)).cuda()
+        ops.m_grouped_fp8_gemm_nt_contiguous(
+            (torch.from_numpy(a).cuda(), torch.from_numpy(a_s).cuda()),
+            (torch.from_numpy(w).cuda(), torch.from_numpy(w_s).cuda()),
+            out, None if use_offsets else torch.from_numpy(mi).cuda(),
+            expert_offsets=offs, silu=silu, tile=128, prefill_pairs=pairs)
+        torch.cuda.synchronize()
+        assert ops.last_device_status() == 0
+        outs.append(out)
+    ref = O.fp8_grouped_gemm(a, a_s, w, w_s, mi, silu=silu)
+    check(outs[0], ref, mi)
+    err = O.rel_err(O.bf16_to_f32(u16(outs[0])), O.bf16_to_f32(u16(outs[1])))
+    assert err["nan"] == 0 and err["max_rel"] <= 2 ** -7, err
+
+
 def test_grouped_gemm_reference_golden(ops):
     """The inputs/outputs of the reference's own cpu_ref_bs (tests/golden)."""
     d = np.load(os.path.join(GOLD, "fp8_v007_ref.npz"))
