@@ -326,6 +326,21 @@ __device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc,
         : "memory");
 }
 
+// Block-scaled pair MMA (kind::mxf8f6f4.block_scale, cta_group::2): each CTA's
+// tensor core reads the scale factors from its own Tensor Memory at the given
+// addresses.  Leader CTA only.
+__device__ __forceinline__ void mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                  uint32_t idesc, uint32_t sfa_tmem,
+                                                  uint32_t sfb_tmem, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "setp.ne.b32 P, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], P;\n\t}" ::
+            "r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
 // Arrive once on the mbarrier at shared::cluster address `cl_bar` (either CTA)
 // when the pair MMAs this thread issued so far are done.
 __device__ __forceinline__ void tc_commit_pair(uint32_t cl_bar) {

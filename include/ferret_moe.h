@@ -56,8 +56,8 @@ extern "C" {
                                        kernels (exact for such scales) */
 #define FERRET_PREFILL_PAIRS 0x4    /* 128-token-tile launches: each expert's whole 256-row chunks
                                        on CTA pairs (tcgen05.mma.cta_group::2, 256x256 tiles),
-                                       the rest on single CTAs; same results, measured slower with
-                                       exact scales (a cross-SM handshake per K block) */
+                                       the rest on single CTAs (with FERRET_UE8M0_SCALES: the
+                                       block-scaled pair kernel); same results, measured slower */
 
 /* Library version (FERRET_MOE_VERSION). */
 FERRET_API int ferret_version(void);

@@ -50,7 +50,7 @@ def test_quant_ue8m0_gather_bit_exact(ops):
     assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
 
 
-def run(ops, a, a_s, w, w_s, mi, silu, ue8m0, use_offsets):
+def run(ops, a, a_s, w, w_s, mi, silu, ue8m0, use_offsets, pairs=False):
     M, K = a.shape
     E, N, _ = w.shape
     out = torch.full((M, N // 2 if silu else N), BF16_NAN, dtype=torch.int16).view(torch.bfloat16).cuda()
@@ -62,7 +62,8 @@ def run(ops, a, a_s, w, w_s, mi, silu, ue8m0, use_offsets):
         (torch.from_numpy(a).cuda(), torch.from_numpy(a_s).cuda()),
         (torch.from_numpy(w).cuda(), torch.from_numpy(w_s).cuda()),
         out, None if use_offsets else torch.from_numpy(mi).cuda(),
-        disable_ue8m0_cast=not ue8m0, expert_offsets=offs, silu=silu, tile=128)
+        disable_ue8m0_cast=not ue8m0, expert_offsets=offs, silu=silu, tile=128,
+        prefill_pairs=pairs)
     torch.cuda.synchronize()
     assert ops.last_device_status() == 0
     return out
@@ -102,6 +103,27 @@ def test_ue8m0_gemm_agrees_with_exact_scale_kernel(ops):
     ex = O.bf16_to_f32(u16(run(ops, a, a_s, w, w_s, mi, False, False, False)))
     err = O.rel_err(mx, ex)
     assert err["nan"] == 0 and err["max_rel"] <= 2 ** -7, err      # one bf16 ulp
+
+
+@pytest.mark.parametrize("seg,N,K", [
+    ([600, 0, 256, 255, 1000, 3], 512, 512),
+    ([1024], 256, 7168),
+    ([513, 770], 1024, 384),
+    ([100, 37], 256, 256),                          # no whole 256-row chunk
+])
+@pytest.mark.parametrize("use_offsets", [False, True])
+def test_ue8m0_gemm_cta_pairs(ops, seg, N, K, use_offsets):
+    """Block-scaled CTA-pair kernel (tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale)
+    on whole 256-row chunks plus the single-CTA block-scaled kernel on the
+    rest: against the fp32 oracle, and within one bf16 ulp of the single-CTA
+    block-scaled kernel alone."""
+    a, a_s, w, w_s, mi = make_case(hash((tuple(seg), N, K, 9)) & 0xFFFF, seg, N, K, 0,
+                                   scale_kind="pow2")
+    out = run(ops, a, a_s, w, w_s, mi, False, True, use_offsets, pairs=True)
+    check(out, O.fp8_grouped_gemm(a, a_s, w, w_s, mi), mi)
+    single = run(ops, a, a_s, w, w_s, mi, False, True, use_offsets)
+    err = O.rel_err(O.bf16_to_f32(u16(out)), O.bf16_to_f32(u16(single)))
+    assert err["nan"] == 0 and err["max_rel"] <= 2 ** -7, err
 
 
 def test_w13_path_ue8m0_prefill_full_size(ops):
