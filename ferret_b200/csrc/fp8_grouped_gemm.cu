@@ -1488,7 +1488,7 @@ int launch_fp8_prefill_mx(const DeviceInfo* info, const void* a, const float* a_
 // that is 32 KB of operands per K block instead of 48 KB for the same MMA
 // work, so the L2->SM stream shrinks by a third and 6 stages fit.
 //
-// Protocol (no multicast loads anywhere):
+// Protocol (every load is a plain TMA load into the issuing CTA's own shared memory):
 //   * both CTAs load their halves with .cta_group::2 TMA, completing on the
 //     leader's (rank 0) full barrier, which the leader arms with both halves'
 //     bytes;
