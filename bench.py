@@ -2,14 +2,19 @@
 """Benchmark of the quantized MoE W13 grouped GEMM hot path (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dsv3_decode]
+                    [--workload ep_prefill] [--no-extras]
 
 One step = one pass of the W13 path over one batch: routing ids -> expert
-permutation -> gathered per-token FP8 quantization -> FP8 block-scaled grouped
-GEMM (bf16 out).  Default workload: DeepSeek-V3 decode W13 (E=256, top-8
-uniform, 128 tokens, K=7168, N=4096), seeded synthetic data and random-init
-weights.  With N>1 GPUs the same global batch is run expert-parallel
-(E/N experts per GPU, NCCL dispatch/combine): strong scaling.
+permutation -> per-token FP8 quantization -> FP8 block-scaled grouped GEMM
+(bf16 out).  Default workload: benchmark configuration 5, the DeepSeek-V3
+prefill W13 batch the metric's 1/2/4/8-GPU sweep is defined on (E=256, top-8
+Zipf(1.1), 32,768 tokens, K=7168, N=4096), seeded synthetic data and
+random-init weights.  With N>1 GPUs the same global batch runs
+expert-parallel (E/N experts per GPU, balanced placement, peer-memory
+dispatch/combine over NVLink): strong scaling.  At N=1, with no --workload,
+the line also carries configurations 2, 3 and 4 (decode, 8,192-token prefill,
+INT4 decode) under "extra_workloads", each timed in the same run with its own
+roofline.
 
 Prints one JSON line on rank 0.  Timing: W untimed warm-up steps, then K
 steps, each bracketed by CUDA events on the launching stream with a 256 MB
@@ -31,6 +36,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 FLUSH_BYTES = 256 << 20
+DEFAULT_WORKLOAD = "ep_prefill"                  # configuration 5 (the 1/2/4/8-GPU sweep)
+EXTRA_WORKLOADS = ("dsv3_decode", "dsv3_prefill", "kimi_int4_decode")   # configurations 2, 3, 4
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -41,9 +48,12 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="dsv3_decode")
+    ap.add_argument("--workload", default=None,
+                    help=f"workload name (default {DEFAULT_WORKLOAD}, plus the extra workloads at N=1)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="N=1 default run: skip the extra workloads")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--placement", choices=["contiguous", "balanced"], default="contiguous",
+    ap.add_argument("--placement", choices=["contiguous", "balanced"], default="balanced",
                     help="expert placement for N>1 (balanced = greedy LPT on the routing histogram)")
     ap.add_argument("--ep-mode", choices=["p2p", "gather", "a2a", "auto"], default="p2p",
                     help="N>1 exchange: p2p = peer-memory kernels (library ferret_ep_*); "
@@ -358,6 +368,7 @@ def run_single(args, cfg):
     counts = (offsets[1:] - offsets[:-1]).tolist()
     byts, flops, active = fp8_algorithmic(cfg, counts)
     ms = sum(step_ms) / len(step_ms)
+    ms_med = statistics.median(step_ms)
     g_ms = sum(gemm_ms) / len(gemm_ms)
     e_ms = sum(e2e_ms) / len(e2e_ms)
     pk = peaks()
@@ -375,6 +386,7 @@ def run_single(args, cfg):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
+        "ms_per_step_median": round(ms_med, 4),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -474,6 +486,7 @@ def run_single_int4(args, cfg):
     counts = torch.bincount(ids.reshape(-1).cpu().long(), minlength=cfg.E).tolist()
     byts, flops, active, wbytes = int4_algorithmic(cfg, counts)
     ms = sum(step_ms) / len(step_ms)
+    ms_med = statistics.median(step_ms)
     g_ms = sum(gemm_ms) / len(gemm_ms)
     e_ms = sum(e2e_ms) / len(e2e_ms)
     pk = peaks()
@@ -482,14 +495,13 @@ def run_single_int4(args, cfg):
         "metric": "grouped W13 GEMM TFLOPS & HBM GB/s vs roofline",
         "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "ms_per_step_median": round(ms_med, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int4 weights dequantized to bf16 x bf16 -> f32 accumulate, bf16 out",
         "data": "synthetic (seeded), random-init weights",
         "config": {"workload": cfg.name, "E": cfg.E, "topk": cfg.topk, "tokens": cfg.T,
                    "routed_rows": cfg.R, "active_experts": active, "K": cfg.K, "N": cfg.N,
                    "silu": cfg.silu, "routing": cfg.routing, "parallelism": "single GPU",
-                   "scales": "ue8m0 (powers of two)" if ue8m0 else "fp32 (exact)",
-                   "prefill_pairs": pairs,
                    "l2": "256 MB flush between timed steps; weights (GBs) exceed L2"},
         "int4_weight_tbs": round(wbytes / (g_ms * 1e-3) / 1e12, 3),
         "roofline": {"bound": "hbm", "kernel": "int4_w13_grouped_kernel",
@@ -509,6 +521,27 @@ def run_single_int4(args, cfg):
     if samples:
         res["cpu_baseline"] = int4_cpu_baseline(hidden, ids, samples, cfg)
     return res
+
+
+def run_extra(args, cfg):
+    """One more single-GPU workload in the same run: its step time (mean and
+    median), value, dominant-kernel roofline and end-to-end figure."""
+    import copy
+    import gc
+    import torch
+    a = copy.copy(args)
+    a.no_cpu_baseline = True
+    gc.collect()
+    torch.cuda.empty_cache()
+    r = run_single(a, cfg)
+    keep = ("value", "unit", "ms_per_step", "ms_per_step_median", "roofline", "e2e", "clocks",
+            "int4_weight_tbs", "hbm_gbs_step")
+    out = {k: r[k] for k in keep if k in r}
+    out["config"] = {k: r["config"][k] for k in ("E", "topk", "tokens", "routed_rows", "K", "N",
+                                                  "silu", "routing") if k in r["config"]}
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -671,7 +704,7 @@ def main():
         print(json.dumps(res), flush=True)
         return
     from ferret_b200.data import CONFIGS
-    cfg = CONFIGS[args.workload]
+    cfg = CONFIGS[args.workload or DEFAULT_WORKLOAD]
     if args.impl == "reference":
         res = run_reference(args, cfg)
     elif args.gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
@@ -679,6 +712,8 @@ def main():
         res = ep_bench.run(args, cfg)
     else:
         res = run_single(args, cfg)
+        if res is not None and args.workload is None and not args.no_extras:
+            res["extra_workloads"] = {name: run_extra(args, CONFIGS[name]) for name in EXTRA_WORKLOADS}
     if res is not None and int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(res), flush=True)
 

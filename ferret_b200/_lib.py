@@ -56,6 +56,7 @@ SIGNATURES = {
     "ferret_ep_connect": (_i, [_p, _p]),
     "ferret_ep_w13_forward": (_i, [_p, _p, _p, _i, _p, _p, _p, _p]),
     "ferret_ep_output_buffer": (_p, [_p]),
+    "ferret_ep_set_events": (_i, [_p, _p, _i]),
     "ferret_ep_destroy": (_i, [_p]),
 }
 

@@ -49,6 +49,18 @@ struct OutMap {
     int total = 0;
     __nv_bfloat16* const* peers = nullptr;
     int peer_rows = 0;
+    // Expert parallelism, prefill kernel only (requires `peers`): the GEMM
+    // pulls its own A rows.  Expert-sorted row i is row
+    // (rows[i] % peer_rows) / gather_topk of rank rows[i] / peer_rows, read
+    // from q_peers (e4m3, K bytes per row) and s_peers (K/128 fp32 scales per
+    // row) and written to row i of the A operand and its scales before any
+    // tile reads it; ready[m] counts the rows landed in 128-row tile m and
+    // must be zero when the launch starts.
+    bool gather = false;
+    const uint8_t* const* q_peers = nullptr;
+    const float* const* s_peers = nullptr;
+    int gather_topk = 0;
+    int* ready = nullptr;
 };
 
 // Workspace for split-K of the swap-AB kernel: tile counters (zeroed before
@@ -59,6 +71,10 @@ struct SplitWs {
     size_t bytes = 0;
     int smax = 1;
 };
+
+// Whether run_fp8_gemm takes the prefill kernel (128-token tiles) for these
+// arguments (rows_hint = expected rows holding data).
+bool fp8_gemm_uses_prefill(int rows_hint, int E, int flags, int N);
 
 // FP8 grouped GEMM launch shared by the entry points: picks the prefill kernel
 // or the swap-AB token tile from rows_hint (expected rows holding data) and E.

@@ -23,6 +23,10 @@
 //   5. grouped GEMM (swap-AB or prefill kernel) whose epilogue writes row i to
 //                   row sorted[i] % (T*topk) of rank sorted[i] / (T*topk)'s
 //                   output buffer                                 (peer stores)
+//      With the prefill kernel (many rows per expert) step 4 happens inside
+//      step 5: copy warps of the GEMM pull the rows in tile order while the
+//      tensor cores work on earlier tiles, and each tile's loads wait for its
+//      rows (per-tile counters, zeroed by the ids kernel of the step).
 //   6. done       : system fence, raise "done(epoch)" on every peer, wait for
 //                   every peer's -- after it every rank's output is complete
 //   7. copy the exported output buffer to the caller's output (optional).
@@ -69,6 +73,8 @@ struct EpDev {
     float* a_s;                         // [world*T*topk, K/128]
     uint32_t* epoch;                    // device step counter
     int* failed;                        // set by a ready barrier that ran out (this step)
+    int* ready;                         // [n_ready] per-tile landed-row counts of the in-GEMM pull
+    int n_ready;
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -143,6 +149,8 @@ __global__ void __launch_bounds__(kGatherThreads)
     const int own = d.T * d.topk;
     const int total = d.world * own;
     const bool failed = *d.failed != 0;
+    for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < d.n_ready; i += gridDim.x * kGatherThreads)
+        d.ready[i] = 0;     // this step's GEMM counts its pulled rows from zero
     for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < total; i += gridDim.x * kGatherThreads) {
         int v = -1;
         if (!failed) {
@@ -214,6 +222,25 @@ __global__ void __launch_bounds__(32, 1) ep_done_kernel(const EpDev d, DevCtl ct
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Records `ev` (if set) on stream s; inside a stream capture as an external
+// record node, so a replayed graph still stamps it.
+int record_event(cudaEvent_t ev, cudaStream_t s) {
+    if (!ev) return FERRET_OK;
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &st) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    const cudaError_t e = st == cudaStreamCaptureStatusActive
+                              ? cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal)
+                              : cudaEventRecord(ev, s);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    return FERRET_OK;
+}
+
 }  // namespace
 }  // namespace ferret
 
@@ -237,6 +264,9 @@ struct ferret_ep {
     size_t perm_ws_bytes = 0;
     uint8_t* a = nullptr;
     float* a_s = nullptr;
+    int* ready = nullptr;               // per-tile counters of the in-GEMM row pull
+    int n_ready = 0;
+    cudaEvent_t ev[4] = {};             // optional step-phase timing events
     uint8_t* peer_base[kMaxRanks] = {};
     bool opened[kMaxRanks] = {};
 };
@@ -337,6 +367,9 @@ extern "C" int ferret_ep_init(int rank, int world, int num_experts, int topk, in
     l = align_up(l + (size_t)pairs * K, 256);
     const size_t off_as = l;
     l = align_up(l + (size_t)pairs * nk * 4, 256);
+    c->n_ready = (int)(pairs / 128 + c->El + 1);   // >= sum over experts of ceil(rows / 128)
+    const size_t off_ready = l;
+    l = align_up(l + (size_t)c->n_ready * 4, 256);
 
     if (cudaMalloc(&c->sym, c->sym_bytes) != cudaSuccess || cudaMalloc(&c->loc, l) != cudaSuccess ||
         cudaMemset(c->sym, 0, c->sym_bytes) != cudaSuccess ||
@@ -354,6 +387,7 @@ extern "C" int ferret_ep_init(int rank, int world, int num_experts, int topk, in
     c->perm_ws = reinterpret_cast<int32_t*>(c->loc + off_pws);
     c->a = c->loc + off_a;
     c->a_s = reinterpret_cast<float*>(c->loc + off_as);
+    c->ready = reinterpret_cast<int*>(c->loc + off_ready);
     cudaIpcMemHandle_t h;
     if (cudaMemcpy(c->remap, remap.data(), remap.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaIpcGetMemHandle(&h, c->sym) != cudaSuccess) {
@@ -471,7 +505,12 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     d.a_s = c->a_s;
     d.epoch = c->epoch;
     d.failed = reinterpret_cast<int*>(c->epoch + 1);
+    d.ready = c->ready;
+    d.n_ready = c->n_ready;
     const DevCtl ctl = make_ctl(info);
+    // the prefill kernel pulls its rows itself (own = the rows one rank receives
+    // on average, the same hint the GEMM's kernel choice uses below)
+    const bool pull_in_gemm = fp8_gemm_uses_prefill(own, c->El, c->flags, c->N);
 
     // 2. publish ids, meet the peers, read every rank's ids
     {
@@ -481,6 +520,7 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
                                 topk_ids)) != FERRET_OK) return rc;
     }
     if ((rc = launch_kernel(ep_ready_kernel, dim3(1), dim3(32), 0, s, d, ctl)) != FERRET_OK) return rc;
+    if ((rc = record_event(c->ev[0], s)) != FERRET_OK) return rc;
     {
         const int want = (pairs + kGatherThreads - 1) / kGatherThreads;
         const int grid = want < info->num_sms * 4 ? want : info->num_sms * 4;
@@ -490,8 +530,8 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     rc = ferret_moe_permute(c->all_ids, c->world * T, c->topk, c->El, c->sorted, c->offsets,
                             c->m_idx, c->perm_ws, c->perm_ws_bytes, stream);
     if (rc != FERRET_OK) return rc;
-    // 4. pull the routed FP8 rows
-    {
+    // 4. pull the routed FP8 rows (inside the GEMM for the prefill kernel)
+    if (!pull_in_gemm) {
         const int want = (pairs + kGatherThreads / 32 - 1) / (kGatherThreads / 32);
         const int grid = want < info->num_sms * 8 ? want : info->num_sms * 8;
         if ((rc = launch_kernel(ep_gather_kernel, dim3(grid), dim3(kGatherThreads), 0, s, d)) != FERRET_OK) return rc;
@@ -502,11 +542,21 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     om.total = pairs;
     om.peers = reinterpret_cast<__nv_bfloat16* const*>(c->tables + 4 * kMaxRanks);
     om.peer_rows = own;
+    if (pull_in_gemm) {
+        om.gather = true;
+        om.q_peers = reinterpret_cast<const uint8_t* const*>(c->tables + 2 * kMaxRanks);
+        om.s_peers = reinterpret_cast<const float* const*>(c->tables + 3 * kMaxRanks);
+        om.gather_topk = c->topk;
+        om.ready = c->ready;
+    }
+    if ((rc = record_event(c->ev[1], s)) != FERRET_OK) return rc;
     rc = run_fp8_gemm(info, c->a, c->a_s, w_fp8, w_scale, my + c->off_out, c->offsets, 0, pairs,
                       c->N, c->K, c->El, c->flags, own, s, om);
     if (rc != FERRET_OK) return rc;
+    if ((rc = record_event(c->ev[2], s)) != FERRET_OK) return rc;
     // 6. every rank's rows have landed
     if ((rc = launch_kernel(ep_done_kernel, dim3(1), dim3(32), 0, s, d, ctl)) != FERRET_OK) return rc;
+    if ((rc = record_event(c->ev[3], s)) != FERRET_OK) return rc;
     // 7. to the caller's buffer
     if (out_bf16 && out_bf16 != my + c->off_out) {
         if (cudaMemcpyAsync(out_bf16, my + c->off_out, (size_t)own * c->n_out * 2,
@@ -515,6 +565,13 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
             return FERRET_ERR_CUDA;
         }
     }
+    return FERRET_OK;
+}
+
+extern "C" int ferret_ep_set_events(ferret_ep* c, void* const* events, int n) {
+    if (!c) return FERRET_ERR_NULL;
+    if (n < 0 || n > 4 || (n > 0 && !events)) return FERRET_ERR_SHAPE;
+    for (int i = 0; i < 4; ++i) c->ev[i] = i < n ? static_cast<cudaEvent_t>(events[i]) : nullptr;
     return FERRET_OK;
 }
 

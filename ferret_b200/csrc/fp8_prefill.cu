@@ -1,0 +1,1029 @@
+// fp8_prefill.cu -- the prefill-shaped FP8 grouped GEMM (tokens on the MMA M
+// axis, 128 x 256 tiles), its staged-store form for outputs on other GPUs
+// (expert parallelism), and the opt-in CTA-pair form.
+#include "fp8_gemm_common.cuh"
+
+namespace ferret {
+namespace {
+
+// REM: only the rows of each expert past its whole 256-row chunks (which the
+// CTA-pair kernel below takes), i.e. its last count % 256 rows.
+template <bool PAIR, bool REM = false>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;                        // 256-row weight tiles
+    const PfLayout L = pf_layout(NS, E, false);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
+    const uint32_t epi_bar = drain_bar + 8u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kPfEpi);
+        }
+        mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kPfEpi);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        if (REM) {
+            s += c & ~255;
+            c &= 255;
+        }
+        seg_s[e] = s;
+        seg_c[e] = c;
+        mt_start[e] = (c + 127) >> 7;
+    }
+    if (seg_bad) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
+            const uint64_t pol_a = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
+                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = stage_base + s * kPfStage;
+                    mbar_expect_tx(full_bar(s), kPfStage);
+                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
+                }
+            }
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (elect_one()) {
+            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
+                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPfStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
+                                   idesc, ks > 0);
+                    tc_commit(empty_bar(s));
+                    tc_commit(tfull_bar(a));
+                }
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else {
+        // ================= epilogue: promotion + store =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        RingPos ra;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int e, row0, rows, nb;
+            decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const bool live = r < rows;
+            const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                       args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(ra.slot));
+            }
+            if (!ok) break;
+            int orow = row0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + row0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            if (live && orow >= 0) {
+                __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
+                if (PAIR) {
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 pk;
+                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                        }
+                        dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// Rows the staged kernel below pulls from the peers itself (expert
+// parallelism; OutMap describes the mapping).  A kernel argument of its own,
+// like SplitArgs, so the tile kernels' argument struct stays as measured.
+struct GatherArgs {
+    const int32_t* src;                 // [rows] global pair index per sorted row; nullptr: no pull
+    const uint8_t* const* q_peers;      // [world] every rank's e4m3 token rows
+    const float* const* s_peers;        // [world] every rank's 1x128 scales
+    uint8_t* a;                         // the A operand: row i is written here
+    float* a_s;                         // its scales
+    int* ready;                         // [128-row tiles] rows landed, zero at launch
+    int own;                            // pairs per rank (tokens * topk)
+    int topk;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy view (the acquire above) before its
+// later async-proxy accesses (the TMA loads of the rows that were pulled).
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until tile counter *cnt reaches `want` rows (acquire).
+__device__ bool wait_rows(const int* cnt, int want, volatile int* abort_flag, const DevCtl& ctl) {
+    if (ld_acquire_gpu(cnt) >= want) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        __nanosleep(128);
+        if (ld_acquire_gpu(cnt) >= want) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > ctl.timeout_ns) {
+            *abort_flag = 1;
+            report(ctl, DEV_TIMEOUT | (SITE_ROWS << 8));
+            return false;
+        }
+    }
+}
+
+// The same kernel for output rows on other GPUs (expert parallelism): rows are
+// written through shared memory, 64 contiguous bytes of 8 rows per store
+// instruction, because 16-byte writes scattered over 32 rows make poor NVLink
+// transactions.  A separate function rather than a template switch of the one
+// above, so that the local kernel's code generation stays as measured.
+//
+// With GatherArgs.src set it also moves the token rows: kPfGatherWarps extra
+// warps per CTA copy the routed rows out of the source ranks' memory (plain
+// 16-byte peer loads, NVLink) into the A operand, in tile order, each landed
+// row counted on its tile's counter (release).  Before the first TMA load of
+// a tile's A rows the producer waits for that count (acquire, then a proxy
+// fence so the async-proxy TMA sees the rows); the epilogue waits the same way
+// before reading the rows' scales.  The pull of later tiles thus runs under
+// the MMAs of earlier ones instead of as a separate kernel before the GEMM.
+// The copy warps wait on nothing, so every count completes while all CTAs are
+// resident (one CTA per SM, grid = SMs); each wait is bounded all the same.
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfPeerThreads, 1)
+    fp8_w13_prefill_peer_kernel(const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
+                           const GatherArgs ga) {
+    pdl_begin();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;                        // 256-row weight tiles
+    const PfLayout L = pf_layout(NS, E, true);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
+    const uint32_t epi_bar = drain_bar + 8u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kPfEpi);
+        }
+        mbar_init(drain_bar, 1);
+        mbar_init(epi_bar, kPfEpi);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfPeerThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        seg_s[e] = s;
+        seg_c[e] = c;
+        mt_start[e] = (c + 127) >> 7;
+    }
+    if (seg_bad) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
+            const uint64_t pol_a = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int e, row0, rows, nb;
+                decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
+                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
+                if (ga.src) {
+                    if (!wait_rows(ga.ready + t / nbc, rows, abort_flag, args.ctl)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_proxy_async_global();
+                }
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = stage_base + s * kPfStage;
+                    mbar_expect_tx(full_bar(s), kPfStage);
+                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
+                }
+            }
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (elect_one()) {
+            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
+                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPfStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
+                                   idesc, ks > 0);
+                    tc_commit(empty_bar(s));
+                    tc_commit(tfull_bar(a));
+                }
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else if (warp >= kPfThreads / 32) {
+        // ================= row pull (expert parallelism) =================
+        if (ga.src) {
+            const int gw = warp - kPfThreads / 32;
+            const int nwarps = gridDim.x * kPfGatherWarps;
+            const int vec = K >> 4;                    // 16-byte words per row
+            const int slots = mt_start[E] * 128;       // 128 row slots per tile, in tile order
+            for (int idx = blockIdx.x * kPfGatherWarps + gw; idx < slots; idx += nwarps) {
+                const int mt = idx >> 7, i = idx & 127;
+                int e, row0, rows, nb;
+                decode_tile<128>(mt, 1, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                if (i >= rows) continue;
+                const int r = row0 + i;
+                const int src = __ldg(ga.src + r);
+                const int g = src / ga.own;
+                const int tok = (src - g * ga.own) / ga.topk;
+                const uint4* q = reinterpret_cast<const uint4*>(ga.q_peers[g] + (size_t)tok * K);
+                const float* sc = ga.s_peers[g] + (size_t)tok * nk;
+                uint4* dst = reinterpret_cast<uint4*>(ga.a + (size_t)r * K);
+                // all of a lane's loads for the row (16 words, 8 KB of the row
+                // per warp pass) before its stores: one NVLink latency per pass
+                for (int base = 0; base < vec; base += 32 * 16) {
+                    uint4 v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int c = base + lane + 32 * j;
+                        if (c < vec) v[j] = __ldcv(q + c);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int c = base + lane + 32 * j;
+                        if (c < vec) dst[c] = v[j];
+                    }
+                }
+                for (int c = lane; c < nk; c += 32) ga.a_s[(size_t)r * nk + c] = __ldcv(sc + c);
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) red_release_gpu_add(ga.ready + mt, 1);
+            }
+        }
+    } else {
+        // ================= epilogue: promotion + store =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint8_t* stg = smem + L.stg_off + (warp - 2) * kPfStgWarp;
+        __nv_bfloat16** rowp = reinterpret_cast<__nv_bfloat16**>(stg + 32 * kPfStgRow);
+        RingPos ra;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int e, row0, rows, nb;
+            decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            if (ga.src && !__all_sync(0xffffffffu,
+                                      wait_rows(ga.ready + t / nbc, rows, abort_flag, args.ctl)))
+                break;
+            const bool live = r < rows;
+            const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldcg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                       args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(ra.slot));
+            }
+            if (!ok) break;
+            int orow = row0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + row0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            // Staged: every store instruction writes 64 contiguous bytes of 8
+            // rows instead of 16 bytes of 32 rows.
+            rowp[lane] = (live && orow >= 0) ? out_row_ptr(args, orow, ldo) : nullptr;
+#pragma unroll
+            for (int k = 0; k < (PAIR ? 2 : 4); ++k) {
+                // chunk k: 32 columns of this thread's row
+                uint4 pk[4];
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    uint32_t* pw = reinterpret_cast<uint32_t*>(&pk[v]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int c = (PAIR ? k * 32 : (k & 1) * 32) + v * 8 + 2 * j;
+                        __nv_bfloat162 b;
+                        if (PAIR)
+                            b = __floats2bfloat162_rn(silu_mul(acc0[c], acc1[c]),
+                                                      silu_mul(acc0[c + 1], acc1[c + 1]));
+                        else if (k < 2)
+                            b = __floats2bfloat162_rn(acc0[c], acc0[c + 1]);
+                        else
+                            b = __floats2bfloat162_rn(acc1[c], acc1[c + 1]);
+                        pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                    }
+                }
+                uint4* srow = reinterpret_cast<uint4*>(stg + lane * kPfStgRow);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) srow[v] = pk[v];
+                __syncwarp();
+                const int col = PAIR ? nb * 128 + h * 64 + k * 32
+                                     : nb * 256 + (k >> 1) * 128 + h * 64 + (k & 1) * 32;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int idx = i * 32 + lane, row = idx >> 2, part = idx & 3;
+                    __nv_bfloat16* o = rowp[row];
+                    if (o)
+                        reinterpret_cast<uint4*>(o + col)[part] =
+                            *reinterpret_cast<const uint4*>(stg + row * kPfStgRow + part * 16);
+                }
+                __syncwarp();
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair form of the prefill kernel (FERRET_PREFILL_PAIRS) for each expert's
+// whole 256-row chunks; the rows past them go to fp8_w13_prefill_kernel<.., true>.
+//
+// A pair (thread-block cluster of 2) computes a 256-token x 256-weight-row
+// tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32): CTA r holds
+// token rows [128r, 128r+128) of the tile and weight rows [128r, 128r+128)
+// (gate block for r = 0 and up block for r = 1 with SiLU), and receives the
+// 128 x 256 partial of its own token rows in its own Tensor Memory.  Per SM
+// that is 32 KB of operands per K block instead of 48 KB for the same MMA
+// work, so the L2->SM stream shrinks by a third and 6 stages fit.
+//
+// Protocol (every load is a plain TMA load into the issuing CTA's own shared memory):
+//   * both CTAs load their halves with .cta_group::2 TMA, completing on the
+//     leader's (rank 0) full barrier, which the leader arms with both halves'
+//     bytes;
+//   * the leader's single MMA thread waits for it, issues the pair MMAs and
+//     commits to each CTA's empty barrier (stage free) and tfull barrier
+//     (K-block partial ready);
+//   * each CTA's 8 epilogue warps promote their own partial exactly as the
+//     single-CTA kernel does and release the buffer with one arrive per warp
+//     on the leader's tempty barrier (16 arrivals);
+//   * a cluster barrier after the roles finish keeps either CTA from leaving
+//     while the other still reads its shared memory or Tensor Memory.
+//
+// Measured on B200 (benchmark configuration 3, GEMM alone): 4.311 ms for this
+// kernel plus the single-CTA remainder launch, against 2.708 ms for the
+// single-CTA kernel alone.  With exact fp32 scales every K block's partial has
+// to be promoted by both CTAs before the leader can reuse one of the two TMEM
+// buffers, which puts a cross-SM round trip (tfull to the peer, the peer's
+// promotion, its arrive back on the leader) on every K block.  Hence opt-in;
+// the pair protocol itself is the base for the block-scaled pair tile, whose
+// single accumulator needs one such handshake per tile.
+// ---------------------------------------------------------------------------
+
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
+    const int nk = K >> 7;
+    const int nbc = N >> 8;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const PpLayout L = pp_layout(NS, E);
+    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
+    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
+    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
+    int* part = reinterpret_cast<int*>(smem + L.part_off);
+    const uint32_t bar0 = smem_addr(smem + L.bar_off);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kPpMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kPpMaxStages + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+    const uint32_t stage_base = smem_addr(smem + L.stages_off);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);            // the leader's arm; bytes from both CTAs
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * (kPfEpi / 32));   // one per epilogue warp of both CTAs
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), 512);
+        tmem_relinquish_pair();
+    }
+    bool seg_bad = false;
+    for (int e = tid; e < E; e += kPfThreads) {
+        int s, c;
+        if (args.seg_pairs) {
+            s = args.seg[2 * e];
+            c = args.seg[2 * e + 1];
+        } else {
+            s = args.seg[e];
+            c = args.seg[e + 1] - s;
+        }
+        if (s < 0 || s > M || c < 0 || c > M - s) {
+            seg_bad = true;
+            s = min(max(s, 0), M);
+            c = min(max(c, 0), M - s);
+        }
+        seg_s[e] = s;
+        seg_c[e] = c & ~255;                      // whole 256-row chunks only
+        mt_start[e] = c >> 8;
+    }
+    if (seg_bad && leader) report(args.ctl, DEV_LAYOUT);
+    __syncthreads();
+    block_exclusive_scan(mt_start, E, part);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                               // both CTAs' barriers are initialised
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = mt_start[E] * nbc;
+
+    if (warp == 0) {
+        // ================= TMA producer (both CTAs) =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_w);
+            tma_prefetch_desc(&tm_a);
+            const uint64_t pol = policy_evict_last();
+            int it = 0;
+            RingPos rp;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                int e, row0, rows, nb;
+                decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const int arow = row0 + 128 * (int)rank;
+                const int wrow = PAIR ? e * N + (rank ? (N >> 1) : 0) + nb * 128
+                                      : e * N + nb * 256 + 128 * (int)rank;
+                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
+                    const int s = rp.slot;
+                    if (!mbar_wait_cl(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl,
+                                      SITE_PEER_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(full_bar(s), 2 * kPpStage);
+                    const uint32_t dst = stage_base + s * kPpStage;
+                    const uint32_t bar = mapa_shared(full_bar(s), 0);
+                    tma_load_2d_pair(dst, &tm_a, kb * 128, arow, bar, pol);
+                    tma_load_2d_pair(dst + 16384, &tm_w, kb * 128, wrow, bar, pol);
+                }
+            }
+            // the last stages are free again once the leader's MMAs consumed
+            // them, which also means this CTA's loads into them have landed
+            for (int i = max(0, it - NS); i < it; ++i)
+                if (!mbar_wait_cl(empty_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl,
+                                  SITE_PEER_TAIL, false))
+                    break;
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer (leader CTA) =================
+        if (leader && elect_one()) {
+            constexpr uint32_t idesc = make_idesc(256, 256, 0, 0);
+            RingPos rs, ra;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                    const int s = rs.slot, a = ra.slot;
+                    if (!mbar_wait_cl(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl,
+                                      SITE_TEMPTY) ||
+                        !mbar_wait_cl(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = stage_base + s * kPpStage;
+                    const uint32_t d = tmem_base + a * 256;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f8f6f4_pair(d, sdesc_k_sw128(st + ks * 32),
+                                        sdesc_k_sw128(st + 16384 + ks * 32), idesc, ks > 0);
+                    tc_commit_pair(empty_bar(s));
+                    tc_commit_pair(mapa_shared(empty_bar(s), 1));
+                    tc_commit_pair(tfull_bar(a));
+                    tc_commit_pair(mapa_shared(tfull_bar(a), 1));
+                }
+            }
+            tc_commit_pair(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
+        }
+    } else {
+        // ================= epilogue: promotion + store (both CTAs) =================
+        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = this CTA's rows
+        const int r = q * 32 + lane;
+        const int ldo = PAIR ? (N >> 1) : N;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        RingPos ra;
+        for (int t = pair; t < total; t += npairs) {
+            int e, row0, rows, nb;
+            decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            const int my0 = row0 + 128 * (int)rank;
+            const bool live = 128 * (int)rank + r < rows;
+            const float* as_row = args.a_scale + (size_t)(my0 + (live ? r : 0)) * nk;
+            const int blk0 = PAIR ? nb : 2 * nb;
+            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
+            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
+            float acc0[64], acc1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                acc0[j] = 0.0f;
+                acc1[j] = 0.0f;
+            }
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
+                ok = __all_sync(0xffffffffu, mbar_wait_cl(tfull_bar(ra.slot), ra.phase, abort_flag,
+                                                          args.ctl, SITE_TFULL));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 16) {
+                    float v[16], u[16];
+                    tmem_ld16(tb + c, v);
+                    tmem_ld16(tb + 128 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(ra.slot), 0));
+            }
+            if (!ok) break;
+            int orow = my0 + r;
+            if (live && args.out_rows) {
+                orow = __ldg(args.out_rows + my0 + r);
+                if (orow < 0 || orow >= args.out_total) orow = -1;
+            }
+            if (live && orow >= 0) {
+                __nv_bfloat16* o = args.out + (size_t)orow * ldo;
+                if (PAIR) {
+                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 pk;
+                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b = __floats2bfloat162_rn(
+                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+                        }
+                        dst[c >> 3] = pk;
+                    }
+                } else {
+                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
+                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 8) {
+                        uint4 p0, p1;
+                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+                        }
+                        d0[c >> 3] = p0;
+                        d1[c >> 3] = p1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                               // the pair's MMAs and arrivals are done
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc_pair(tmem_base, 512);
+    }
+}
+
+template <bool PAIR>
+int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const float* a_scale,
+                             const void* w, const float* w_scale, void* out, const int32_t* seg,
+                             int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
+                             const OutMap& om) {
+    CUtensorMap tm_w, tm_a;
+    int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
+                          128, true);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
+    if (rc != FERRET_OK) return rc;
+    const int budget = info->max_smem_optin - 1024;
+    const int stages = std::min(kPpMaxStages, (budget - pp_layout(0, E).total) / kPpStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const int smem = pp_layout(stages, E).total + 1024;
+    auto kern = fp8_w13_prefill_pair_kernel<PAIR>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    const int pairs = std::min(max_resident_pairs(kern, dim3(kPfThreads), smem), info->num_sms / 2);
+    if (pairs < 1) return FERRET_ERR_UNSUPPORTED;
+    GemmArgs g;
+    g.a_scale = a_scale;
+    g.w_scale = w_scale;
+    g.seg = seg;
+    g.seg_pairs = seg_pairs;
+    g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_rows = om.rows;
+    g.out_total = om.total;
+    g.out_peers = nullptr;
+    g.peer_rows = 0;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.E = E;
+    g.stages = stages;
+    g.ctl = make_ctl(info);
+    rc = launch_kernel_pairs(kern, dim3(2 * pairs), dim3(kPfThreads), smem, stream, tm_w, tm_a, g);
+    if (rc != FERRET_OK) return rc;
+    // the rows past each expert's whole 256-row chunks
+    const int stages1 = std::min(kPfMaxStages, (budget - pf_layout(0, E, false).total) / kPfStage);
+    if (stages1 < 2) return FERRET_ERR_SHAPE;
+    const int smem1 = pf_layout(stages1, E, false).total + 1024;
+    auto kern1 = fp8_w13_prefill_kernel<PAIR, true>;
+    if (cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    g.stages = stages1;
+    return launch_kernel(kern1, dim3(info->num_sms), dim3(kPfThreads), smem1, stream, tm_w, tm_a, g);
+}
+
+
+template <bool PAIR, bool STAGED>
+int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
+    CUtensorMap tm_w, tm_a;
+    int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
+                          128, true);
+    if (rc != FERRET_OK) return rc;
+    rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
+    if (rc != FERRET_OK) return rc;
+    const int budget = info->max_smem_optin - 1024;
+    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E, STAGED).total) / kPfStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const int smem = pf_layout(stages, E, STAGED).total + 1024;
+    auto kern_local = fp8_w13_prefill_kernel<PAIR>;
+    auto kern_peer = fp8_w13_prefill_peer_kernel<PAIR>;
+    const cudaError_t ae =
+        STAGED ? cudaFuncSetAttribute(kern_peer, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+               : cudaFuncSetAttribute(kern_local, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (ae != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    GemmArgs g;
+    g.a_scale = a_scale;
+    g.w_scale = w_scale;
+    g.seg = seg;
+    g.seg_pairs = seg_pairs;
+    g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_rows = om.rows;
+    g.out_total = om.total;
+    g.out_peers = om.peers;
+    g.peer_rows = om.peer_rows;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.E = E;
+    g.stages = stages;
+    g.ctl = make_ctl(info);
+    if (!STAGED) return launch_kernel(kern_local, dim3(info->num_sms), dim3(kPfThreads), smem, stream,
+                                      tm_w, tm_a, g);
+    GatherArgs ga = {};
+    if (om.gather) {
+        if (!om.rows || !om.q_peers || !om.s_peers || !om.ready || om.peer_rows <= 0 ||
+            om.gather_topk <= 0)
+            return FERRET_ERR_NULL;
+        ga.src = om.rows;
+        ga.q_peers = om.q_peers;
+        ga.s_peers = om.s_peers;
+        ga.a = static_cast<uint8_t*>(const_cast<void*>(a));
+        ga.a_s = const_cast<float*>(a_scale);
+        ga.ready = om.ready;
+        ga.own = om.peer_rows;
+        ga.topk = om.gather_topk;
+    }
+    return launch_kernel(kern_peer, dim3(info->num_sms), dim3(kPfPeerThreads), smem, stream, tm_w,
+                         tm_a, g, ga);
+}
+
+template <bool PAIR>
+int launch_fp8_prefill_p(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
+                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
+    return om.peers ? launch_fp8_prefill_t<PAIR, true>(info, a, a_scale, w, w_scale, out, seg,
+                                                       seg_pairs, M, N, K, E, stream, om)
+                    : launch_fp8_prefill_t<PAIR, false>(info, a, a_scale, w, w_scale, out, seg,
+                                                        seg_pairs, M, N, K, E, stream, om);
+}
+
+}  // namespace
+
+int launch_fp8_prefill(bool pair, const DeviceInfo* info, const void* a, const float* a_scale,
+                       const void* w, const float* w_scale, void* out, const int32_t* seg,
+                       int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
+                       const OutMap& om) {
+    return pair ? launch_fp8_prefill_p<true>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
+                                             N, K, E, stream, om)
+                : launch_fp8_prefill_p<false>(info, a, a_scale, w, w_scale, out, seg, seg_pairs, M,
+                                              N, K, E, stream, om);
+}
+
+int launch_fp8_prefill_pairs(bool pair, const DeviceInfo* info, const void* a,
+                             const float* a_scale, const void* w, const float* w_scale, void* out,
+                             const int32_t* seg, int seg_pairs, int M, int N, int K, int E,
+                             cudaStream_t stream, const OutMap& om) {
+    return pair ? launch_fp8_prefill_pairs_p<true>(info, a, a_scale, w, w_scale, out, seg,
+                                                   seg_pairs, M, N, K, E, stream, om)
+                : launch_fp8_prefill_pairs_p<false>(info, a, a_scale, w, w_scale, out, seg,
+                                                    seg_pairs, M, N, K, E, stream, om);
+}
+
+}  // namespace ferret

@@ -122,18 +122,32 @@ def per_block_cast_to_fp8(w: torch.Tensor, use_ue8m0: bool = False):
 
 
 def fp8_weights(E: int, N: int, K: int, seed: int = SEED_WEIGHTS, device="cpu",
-                std: float = 0.02, chunk: int = 8, use_ue8m0: bool = False):
-    """Random-init FP8 expert weights, generated on `device` in expert chunks."""
-    w_q = torch.empty(E, N, K, dtype=torch.float8_e4m3fn, device=device)
-    w_s = torch.empty(E, N // 128, K // 128, dtype=torch.float32, device=device)
+                std: float = 0.02, chunk: int = 8, use_ue8m0: bool = False, select=None):
+    """Random-init FP8 expert weights, generated on `device` in expert chunks.
+
+    `select` (a sequence of expert ids) keeps only those experts, in that
+    order, with the values they have in the full E-expert set: every chunk is
+    still drawn from the one generator, so an expert-parallel rank holding a
+    shard sees exactly the weights a single GPU holding all E would."""
+    keep = list(range(E)) if select is None else [int(e) for e in select]
+    slot = {}
+    for i, e in enumerate(keep):
+        slot.setdefault(e, []).append(i)
+    w_q = torch.empty(len(keep), N, K, dtype=torch.float8_e4m3fn, device=device)
+    w_s = torch.empty(len(keep), N // 128, K // 128, dtype=torch.float32, device=device)
     g = _gen(seed, device)
     for e0 in range(0, E, chunk):
         e1 = min(E, e0 + chunk)
         w = torch.randn(e1 - e0, N, K, generator=g, device=device) * std
+        if not any(e in slot for e in range(e0, e1)):
+            del w
+            continue
         q, s = per_block_cast_to_fp8(w, use_ue8m0)
-        w_q[e0:e1] = q
-        w_s[e0:e1] = s
-        del w
+        for e in range(e0, e1):
+            for i in slot.get(e, ()):
+                w_q[i] = q[e - e0]
+                w_s[i] = s[e - e0]
+        del w, q, s
     return w_q, w_s
 
 

@@ -155,6 +155,19 @@ class PeerContext:
               "ferret_ep_w13_forward")
         return out
 
+    def set_events(self, events):
+        """Step-phase timing events the library records in every later step
+        (ferret_ep_set_events): after the ready barrier, before and after the
+        GEMM, after the done barrier.  An empty list turns them off."""
+        from ._lib import check
+        for e in events:
+            e.record()              # torch creates the CUDA event on first record
+        torch.cuda.synchronize()
+        self._events = list(events)
+        arr = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in events])
+        check(self.L.ferret_ep_set_events(self.ctx, ctypes.cast(arr, ctypes.c_void_p), len(events)),
+              "ferret_ep_set_events")
+
     def close(self):
         """Collective: waits for this rank's work, meets the peers, frees."""
         if self.ctx is None:
@@ -213,6 +226,14 @@ class ExpertParallelW13:
         self.peer = None
         if mode == "p2p" and not (W_local.is_cuda and isinstance(self.kernels, CudaKernels)):
             raise ValueError("mode 'p2p' runs the CUDA library on GPU-resident weights")
+
+    def set_phase_events(self, events):
+        """Mode "p2p": up to 4 timing events recorded inside every later step
+        (after the ready barrier, before and after the GEMM, after the done
+        barrier).  Needs a first step to have created the peer context."""
+        if self.peer is None:
+            raise RuntimeError("set_phase_events needs the p2p context (run a step first)")
+        self.peer.set_events(events)
 
     def close(self):
         """Collective: releases the peer-memory context (mode "p2p")."""

@@ -228,14 +228,18 @@ FERRET_API size_t ferret_fp8_grouped_gemm_workspace_size(int M, int E);
  * allocate device memory when they call -- a serving process that has handed
  * almost all HBM to weights and the KV cache, or a plugin host that reaches
  * this library through an FFI and has no access to its framework's allocator.
- * Same arguments and results as the workspace entry point with
- * expert_offsets = NULL, minus the workspace: the per-expert segments derived
+ * Same arguments as the workspace entry point with expert_offsets = NULL,
+ * minus the workspace, and the same kernel choice; results agree with that
+ * entry point within the GEMM's tolerance, not always bit for bit (without a
+ * workspace there is no split-K, which the workspace entry point uses for
+ * launches with few tiles).  The per-expert segments derived
  * from m_indices live in a fixed 8 KB device array inside this library
  * (2 x 1024 int32), which every GPU that loads the library keeps until the
  * process exits.  It allocates nothing and calls no allocator.
  * Limit: E <= 1024 (the array's size); larger E returns FERRET_ERR_SHAPE.
  * The first call on a device looks up the array's device address with that
- * device current; make that first call before any stream capture.
+ * device current; make that first call before any stream capture (a lookup
+ * that fails returns FERRET_ERR_CUDA and is retried by the next call).
  * All calls share the one array and each call rewrites the entries it uses
  * before reading them; calls that overlap on the GPU (e.g. on two streams at
  * once) race on it and must be serialised by the caller.
@@ -338,6 +342,16 @@ FERRET_API int ferret_ep_w13_forward(ferret_ep* ctx, const void* hidden_bf16, co
                                      int T, const void* w_fp8, const float* w_scale, void* out_bf16,
                                      void* stream);
 FERRET_API void* ferret_ep_output_buffer(ferret_ep* ctx);
+/*
+ * Optional step-phase timing: up to 4 cudaEvent_t handles (passed as void*,
+ * created by the caller with timing enabled) that every later
+ * ferret_ep_w13_forward records on its stream -- [0] after the ready barrier,
+ * [1] before the grouped GEMM (after the permutation and, for decode-sized
+ * batches, the separate row pull), [2] after the GEMM, [3] after the done
+ * barrier.  Inside a stream capture they become external record nodes, so a
+ * replayed graph stamps them.  n = 0 turns the recording off.
+ */
+FERRET_API int ferret_ep_set_events(ferret_ep* ctx, void* const* events, int n);
 FERRET_API int ferret_ep_destroy(ferret_ep* ctx);
 
 #ifdef __cplusplus

@@ -66,36 +66,44 @@ def _worker(rank, world, port, q):
         cases += [(None, "p2p", True), (bal, "p2p", True)]
         cases += [("big", "p2p", False), ("big", "p2p", True)]   # prefill kernel, peer stores
         # a batch large enough (> 48 rows per local expert) for the prefill kernel
+        # (its GEMM pulls the rows from the peers itself); consecutive steps
+        # alternate between two token batches, so a tile that read rows left
+        # over from the previous step would show
         Tb = 1024
-        hidden_b = data.activations(Tb, K, seed=11).to(dev)
         ids_b = data.routing(Tb, E, topk, "zipf").to(dev)
-        refs_b = {}
-        for silu in (False, True):
-            out, rows, _ = ops.fp8_moe_w13(hidden_b, ids_b, W, Ws, silu=silu)
-            ref = torch.zeros(Tb * topk, out.shape[1], dtype=out.dtype, device=dev)
-            ref[rows.long()] = out
-            refs_b[silu] = ref
+        hidden_bs = [data.activations(Tb, K, seed=sd).to(dev) for sd in (11, 12)]
+        refs_bs = []
+        for hb in hidden_bs:
+            refs_b = {}
+            for silu in (False, True):
+                out, rows, _ = ops.fp8_moe_w13(hb, ids_b, W, Ws, silu=silu)
+                ref = torch.zeros(Tb * topk, out.shape[1], dtype=out.dtype, device=dev)
+                ref[rows.long()] = out
+                refs_b[silu] = ref
+            refs_bs.append(refs_b)
         El = E // world
         results = []
         for placement, mode, silu in cases:
             big = isinstance(placement, str)
             if big:
                 placement = None
-            Tn, hid_n, ids_n, refs_n = (Tb, hidden_b, ids_b, refs_b) if big else (T, hidden, ids, refs)
+            Tn, hids, ids_n, refs_l = ((Tb, hidden_bs, ids_b, refs_bs) if big
+                                       else (T, [hidden], ids, [refs]))
             Tl = Tn // world
-            h_loc = hid_n[rank * Tl:(rank + 1) * Tl].contiguous()
+            h_locs = [h[rank * Tl:(rank + 1) * Tl].contiguous() for h in hids]
             i_loc = ids_n[rank * Tl:(rank + 1) * Tl].contiguous()
             table = placement if placement is not None else torch.arange(E)
             mine = table[rank * El:(rank + 1) * El].long().to(dev)
             ep = ExpertParallelW13(W[mine].contiguous(), Ws[mine].contiguous(), E, placement=placement,
                                    mode=mode, silu=silu, max_tokens=2 * Tl)
-            want = refs_n[silu][rank * Tl * topk:(rank + 1) * Tl * topk]
+            wants = [r[silu][rank * Tl * topk:(rank + 1) * Tl * topk] for r in refs_l]
             steps = 3 if mode == "p2p" else 1      # several epochs through one context
             ok = True
-            for _ in range(steps):
-                got = ep.forward(h_loc, i_loc)
+            for i in range(steps):
+                got = ep.forward(h_locs[i % len(h_locs)], i_loc)
                 torch.cuda.synchronize()
-                ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
+                ok = ok and torch.equal(got.view(torch.int16), wants[i % len(wants)].view(torch.int16))
+            h_loc, want = h_locs[0], wants[0]
             if mode == "p2p" and silu:
                 # the same step replayed from a CUDA graph
                 side = torch.cuda.Stream()

@@ -356,10 +356,20 @@ def test_w13_path_cpu_config(ops, silu):
     assert err["nan"] == 0 and err["max_rel"] < TOL, err
 
 
+def _torch_ref(q, s, W, Ws, e, silu=False):
+    """fp32 dequantize-then-matmul of one expert's rows on the host cores
+    (oracle.fp8_w13_torch_cpu, checked against the scalar oracle on the CPU)."""
+    n = q.shape[0]
+    res = O.fp8_w13_torch_cpu(torch.from_numpy(q), torch.from_numpy(s), W[e:e + 1].cpu(),
+                              Ws[e:e + 1].cpu(), [0, n], [0], silu=silu)
+    return res[0].numpy()
+
+
 def test_w13_path_dsv3_decode_full_size(ops):
-    """Benchmark configuration 2 at full size; every output row of 48 sampled experts
-    is checked against the fp32 oracle, permutation and quantization in full."""
+    """Benchmark configuration 2 at full size: every output row of every active
+    expert against the fp32 oracle; permutation and quantization in full."""
     from ferret_b200 import data
+    torch.set_num_threads(os.cpu_count() or 1)
     cfg = data.CONFIGS["dsv3_decode"]
     dev = torch.device("cuda")
     W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
@@ -373,16 +383,46 @@ def test_w13_path_dsv3_decode_full_size(ops):
     q, s = O.quant_act_fp8_1x128(u16(hidden), r_rows, cfg.topk)
     qd, sd = ops.per_token_cast_to_fp8(hidden.cuda(), rows, cfg.topk)
     assert np.array_equal(u8(qd), q)
-    rng = np.random.default_rng(0)
-    experts = rng.choice(np.nonzero(np.diff(r_offs))[0], 48, replace=False)
     got = O.bf16_to_f32(u16(out))
+    experts = np.nonzero(np.diff(r_offs))[0]
+    assert len(experts) == 252
     for e in experts:
         r0, r1 = r_offs[e], r_offs[e + 1]
-        ref = O.fp8_grouped_gemm_fast(q[r0:r1], s[r0:r1], u8(W[e:e + 1]), Ws[e:e + 1].cpu().numpy(),
-                                      np.zeros(r1 - r0, np.int32))
-        err = O.rel_err(got[r0:r1], ref)
+        err = O.rel_err(got[r0:r1], _torch_ref(q[r0:r1], s[r0:r1], W, Ws, e))
         assert err["nan"] == 0 and err["max_rel"] < TOL, (int(e), err)
     assert ops.last_device_status() == 0
+
+
+def test_w13_path_ep_prefill_full_size(ops):
+    """Benchmark configuration 5's global batch on one GPU (E=256, top-8
+    Zipf(1.1), 32,768 tokens = 262,144 routed rows, K=7168, N=4096): the
+    permutation in full, and every row of the 6 largest experts (28,497 rows
+    down to 8,259) and of 10 random other active experts against the fp32
+    oracle, quantized by the oracle's own quantizer."""
+    from ferret_b200 import data
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = data.CONFIGS["ep_prefill"]
+    dev = torch.device("cuda")
+    W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)
+    hidden = data.activations(cfg.T, cfg.K)
+    ids = data.routing(cfg.T, cfg.E, cfg.topk, cfg.routing, cfg.zipf_s)
+    out, rows, offs = ops.fp8_moe_w13(hidden.cuda(), ids.cuda(), W, Ws)
+    torch.cuda.synchronize()
+    assert ops.last_device_status() == 0
+    r_rows, r_offs, _ = O.moe_permute(ids.numpy(), cfg.E)
+    assert np.array_equal(rows.cpu().numpy(), r_rows)
+    assert np.array_equal(offs.cpu().numpy(), r_offs)
+    counts = np.diff(r_offs)
+    order = np.argsort(-counts, kind="stable")
+    rest = [e for e in order[6:] if counts[e] > 0]
+    experts = list(order[:6]) + list(np.random.default_rng(5).choice(rest, 10, replace=False))
+    h = u16(hidden)
+    for e in experts:
+        r0, r1 = int(r_offs[e]), int(r_offs[e + 1])
+        q, s = O.quant_act_fp8_1x128(h, r_rows[r0:r1], cfg.topk)
+        got = O.bf16_to_f32(u16(out[r0:r1]))
+        err = O.rel_err(got, _torch_ref(q, s, W, Ws, e))
+        assert err["nan"] == 0 and err["max_rel"] < TOL, (int(e), r1 - r0, err)
 
 
 # ---------------------------------------------------------------- expert parallel, one rank

@@ -196,6 +196,45 @@ def test_fast_and_scalar_int4_oracles_agree():
         assert O.rel_err(fast, ref)["max_rel"] < 1e-4
 
 
+def test_torch_cpu_fp8_path_agrees_with_scalar_oracle():
+    """The torch fp32 path (the timed CPU baseline, also the per-expert checker
+    of the full-size GPU tests) against the scalar oracle."""
+    import torch
+    rng = np.random.default_rng(4)
+    M, N, K, E = 24, 256, 384, 3
+    a = O.f32_to_e4m3(rng.standard_normal((M, K)).astype(np.float32) * 50)
+    w = O.f32_to_e4m3(rng.standard_normal((E, N, K)).astype(np.float32) * 50)
+    a_s = rng.uniform(0.001, 0.01, (M, K // 128)).astype(np.float32)
+    w_s = rng.uniform(0.001, 0.01, (E, N // 128, K // 128)).astype(np.float32)
+    mi = np.sort(rng.integers(0, E, M)).astype(np.int32)
+    offs = np.concatenate([[0], np.cumsum(np.bincount(mi, minlength=E))])
+    for silu in (False, True):
+        ref = O.fp8_grouped_gemm(a, a_s, w, w_s, mi, silu=silu)
+        got = O.fp8_w13_torch_cpu(torch.from_numpy(a), torch.from_numpy(a_s), torch.from_numpy(w),
+                                  torch.from_numpy(w_s), offs, range(E), silu=silu)
+        for e in range(E):
+            if offs[e + 1] > offs[e]:
+                assert O.rel_err(got[e].numpy(), ref[offs[e]:offs[e + 1]])["max_rel"] < 1e-4
+
+
+def test_torch_cpu_int4_path_agrees_with_scalar_oracle():
+    import sys
+    import torch
+    sys.path.insert(0, GOLD)
+    import make_golden as G
+    h, rq, sc, ids = G.int4_inputs(11, T=4, E=3, K=256, N=256, topk=2)
+    flat = ids.reshape(-1)
+    for silu in (False, True):
+        ref = O.int4_w13(h, rq, sc, ids, silu=silu)
+        for e in np.unique(flat):
+            pairs = np.nonzero(flat == e)[0]
+            x = torch.from_numpy(h.view(np.int16)).view(torch.bfloat16)[torch.from_numpy(pairs // 2)]
+            got = O.int4_w13_torch_cpu(x, torch.from_numpy(rq[e]),
+                                       torch.from_numpy(sc[e].view(np.int16)).view(torch.bfloat16),
+                                       silu=silu)
+            assert O.rel_err(got.numpy(), ref[pairs])["max_rel"] < 1e-4
+
+
 def test_rel_err_counts_nan():
     r = O.rel_err(np.array([1.0, np.nan]), np.array([1.0, 2.0]))
     assert r["nan"] == 1 and r["max_rel"] == np.inf
