@@ -40,7 +40,7 @@
 // bf16x2 multiply by the scale rounds once -- the oracle's bf16((n-8)*s).
 #include <algorithm>
 
-#include "capi_internal.h"
+#include "int4_common.cuh"
 
 namespace ferret {
 namespace {
@@ -108,36 +108,6 @@ __host__ __device__ inline I4Layout i4_layout(int stage_bytes, int stages, int E
     o += 16;
     L.total = o;
     return L;
-}
-
-__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-// One repacked word (slots hold k offsets 0,2,4,6,1,3,5,7) and the scale
-// pair (s, s) -> 8 bf16 weights for k offsets 0..7, as four bf16x2 words.
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2) {
-    const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u, kBias = 0x43084308u;  // 128, 136
-    uint4 r;
-    r.x = bf16x2_mul(bf16x2_sub(lop3_and_or(w, kMask, kMagic), kBias), s2);
-    r.y = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 4, kMask, kMagic), kBias), s2);
-    r.z = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 8, kMask, kMagic), kBias), s2);
-    r.w = bf16x2_mul(bf16x2_sub(lop3_and_or(w >> 12, kMask, kMagic), kBias), s2);
-    return r;
 }
 
 template <int NT>
@@ -676,6 +646,12 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
     const int R = T * topk;
     const uint8_t* blob = static_cast<const uint8_t*>(w_blob);
     int nt = (flags >> FERRET_TILE_SHIFT) & 0xFF;
+    // A few rows per active expert (at most 4 on average, counting every
+    // expert that can be active): the register-dequant decode kernel, which
+    // streams the weights once without materialising them; more rows, or a
+    // forced token tile: the tensor-core kernel.
+    const bool decode = nt == 0 && R > kSplitMaxRows && (long long)R <= 4ll * std::min(R, E) &&
+                        (reinterpret_cast<uintptr_t>(out_bf16) & 7u) == 0;
     if (nt == 0) {
         const int avg = (R + E - 1) / E;
         nt = avg <= 4 ? 8 : avg <= 12 ? 16 : 32;
@@ -688,7 +664,9 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
     if (R <= kSplitMaxRows && ws_bytes > rows_bytes) {
         split_ws = static_cast<uint8_t*>(workspace) + rows_bytes;
         split_bytes = ws_bytes - rows_bytes;
-        const long long tiles_up = ((long long)std::min(R, E) + R / std::max(nt, 1)) * (pair ? N / 256 : N / 128);
+        const long long tiles_up =
+            decode ? int4_decode_items_bound(R, E, N, pair)
+                   : ((long long)std::min(R, E) + R / std::max(nt, 1)) * (pair ? N / 256 : N / 128);
         ncnt = (int)std::min<long long>(tiles_up, (long long)(split_bytes / sizeof(int)));
     }
     {
@@ -699,6 +677,9 @@ extern "C" int ferret_int4_moe_w13(const void* hidden_bf16, const void* w_blob,
                                 static_cast<uint4*>(workspace), reinterpret_cast<int*>(split_ws),
                                 ncnt, make_ctl(info))) != FERRET_OK) return rc;
     }
+    if (decode)
+        return launch_int4_decode(info, workspace, blob, sorted_rows, expert_offsets, out_bf16, T,
+                                  topk, N, K, E, R, pair, s, split_ws, split_bytes, ncnt);
 #define FERRET_I4_CASE(NT_)                                                                        \
     case NT_:                                                                                      \
         return pair ? launch_int4<NT_, true>(info, workspace, blob, sorted_rows, expert_offsets,   \

@@ -71,7 +71,7 @@ def _parity(cfg, ids_g, hidden_g, out_local, rank, G, Tl, dev):
     rows_local = torch.arange(0, Tl * cfg.topk, PARITY_STRIDE, device=dev)
     mine = out_local.index_select(0, rows_local).contiguous()
     allv = torch.empty(G * mine.shape[0], mine.shape[1], dtype=mine.dtype, device=dev)
-    dist.all_gather_into_tensor(allv.view(torch.int16), mine.view(torch.int16))
+    dist.all_gather_into_tensor(allv, mine)      # bf16 (NCCL has no int16)
     res = None
     if rank == 0:
         W, Ws = data.fp8_weights(cfg.E, cfg.N, cfg.K, device=dev)

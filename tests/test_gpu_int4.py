@@ -93,6 +93,32 @@ def test_int4_vs_oracle(ops, T, E, K, N, topk, silu, tile):
     assert not got[~valid].any()
 
 
+@pytest.mark.parametrize("T,E,K,N,topk,silu,skew", [
+    (1, 8, 256, 256, 8, True, False),
+    (3, 5, 384, 256, 2, False, False),
+    (8, 16, 512, 512, 4, True, False),
+    (40, 64, 256, 256, 2, False, True),  # one expert with 27 rows: four 8-row passes
+    (40, 64, 512, 512, 2, True, True),
+    (64, 384, 1024, 256, 8, False, False),
+])
+def test_int4_decode_kernel_vs_oracle(ops, T, E, K, N, topk, silu, skew):
+    """The register-dequant decode kernel (chosen automatically when the routed
+    rows average at most 4 per possibly-active expert): all pairs against the
+    oracle, dropped pairs untouched, experts with more rows than one 8-row pass."""
+    h, rq, sc, ids = inputs(T * 5 + E, T, E, K, N, topk)
+    ids = ids.copy()
+    if skew:
+        ids[:27, 0] = 3                  # expert 3 in slot 0 of the first 27 tokens
+        ids[:27, 1] = np.where(ids[:27, 1] == 3, 4, ids[:27, 1])
+    ids[0, -1] = -1
+    got = run(ops, h, rq, sc, ids, silu, 0)
+    ref = O.int4_w13(h, rq, sc, ids, silu=silu)
+    valid = ids.reshape(-1) >= 0
+    err = O.rel_err(got[valid], ref[valid])
+    assert err["nan"] == 0 and err["max_rel"] < TOL, err
+    assert not got[~valid].any()
+
+
 @pytest.mark.parametrize("T,E,K,N,topk,silu", [
     (1, 384, 7168, 512, 8, True),        # the reference's TP8 T=1 shape
     (2, 16, 2048, 256, 4, False),
@@ -154,6 +180,11 @@ def test_int4_kimi_decode_full_size(ops):
         out = ops.moe_wna16_w13(hidden.to(dev), packed, ids.to(dev), silu=silu)
         torch.cuda.synchronize()
         outs[silu] = O.bf16_to_f32(u16(out))
+        # the tensor-core kernel (forced 8-row token tile) on the same inputs
+        tc = ops.moe_wna16_w13(hidden.to(dev), packed, ids.to(dev), silu=silu, tile=8)
+        torch.cuda.synchronize()
+        err = O.rel_err(O.bf16_to_f32(u16(tc)), outs[silu])
+        assert err["nan"] == 0 and err["max_rel"] < TOL, ("tensor-core vs decode", silu, err)
     for e in experts:
         pairs = np.nonzero(flat == e)[0]
         raw_e, sc_e = raw[e].cpu(), sc[e].cpu()
