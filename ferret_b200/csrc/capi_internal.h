@@ -49,18 +49,21 @@ struct OutMap {
     int total = 0;
     __nv_bfloat16* const* peers = nullptr;
     int peer_rows = 0;
-    // Expert parallelism, prefill kernel only (requires `peers`): the GEMM
-    // pulls its own A rows.  Expert-sorted row i is row
+    // Expert parallelism, prefill kernel only (requires `rows` and `peers`):
+    // the GEMM moves the rows itself.  Expert-sorted row i is row
     // (rows[i] % peer_rows) / gather_topk of rank rows[i] / peer_rows, read
     // from q_peers (e4m3, K bytes per row) and s_peers (K/128 fp32 scales per
-    // row) and written to row i of the A operand and its scales before any
-    // tile reads it; ready[m] counts the rows landed in 128-row tile m and
-    // must be zero when the launch starts.
+    // row) into row i of the A operand and its scales before any tile reads
+    // it; the tiles are stored to row i of `out` (a local staging matrix) and
+    // then copied to row rows[i] % peer_rows of peers[rows[i] / peer_rows].
+    // ready[m] / done[m] count rows landed / warp-tiles stored for 128-row
+    // tile m and must be zero when the launch starts.
     bool gather = false;
     const uint8_t* const* q_peers = nullptr;
     const float* const* s_peers = nullptr;
     int gather_topk = 0;
     int* ready = nullptr;
+    int* done = nullptr;
 };
 
 // Workspace for split-K of the swap-AB kernel: tile counters (zeroed before

@@ -23,10 +23,12 @@
 //   5. grouped GEMM (swap-AB or prefill kernel) whose epilogue writes row i to
 //                   row sorted[i] % (T*topk) of rank sorted[i] / (T*topk)'s
 //                   output buffer                                 (peer stores)
-//      With the prefill kernel (many rows per expert) step 4 happens inside
-//      step 5: copy warps of the GEMM pull the rows in tile order while the
-//      tensor cores work on earlier tiles, and each tile's loads wait for its
-//      rows (per-tile counters, zeroed by the ids kernel of the step).
+//      With the prefill kernel (many rows per expert) steps 4 and 5 are one
+//      kernel: a mover warp per CTA pulls the rows in tile order while the
+//      tensor cores work on earlier tiles (each tile's loads wait for its
+//      rows), the tiles are stored to a local staging matrix, and a second
+//      mover warp copies each finished 128-row tile's rows to the source
+//      ranks as whole rows (per-tile counters, zeroed by the ids kernel).
 //   6. done       : system fence, raise "done(epoch)" on every peer, wait for
 //                   every peer's -- after it every rank's output is complete
 //   7. copy the exported output buffer to the caller's output (optional).
@@ -74,6 +76,7 @@ struct EpDev {
     uint32_t* epoch;                    // device step counter
     int* failed;                        // set by a ready barrier that ran out (this step)
     int* ready;                         // [n_ready] per-tile landed-row counts of the in-GEMM pull
+    int* done;                          // [n_ready] per-tile stored-warp counts for the in-GEMM push
     int n_ready;
 };
 
@@ -149,8 +152,10 @@ __global__ void __launch_bounds__(kGatherThreads)
     const int own = d.T * d.topk;
     const int total = d.world * own;
     const bool failed = *d.failed != 0;
-    for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < d.n_ready; i += gridDim.x * kGatherThreads)
-        d.ready[i] = 0;     // this step's GEMM counts its pulled rows from zero
+    for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < d.n_ready; i += gridDim.x * kGatherThreads) {
+        d.ready[i] = 0;     // this step's GEMM counts its pulled rows and stored tiles from zero
+        d.done[i] = 0;
+    }
     for (int i = blockIdx.x * kGatherThreads + threadIdx.x; i < total; i += gridDim.x * kGatherThreads) {
         int v = -1;
         if (!failed) {
@@ -265,7 +270,9 @@ struct ferret_ep {
     uint8_t* a = nullptr;
     float* a_s = nullptr;
     int* ready = nullptr;               // per-tile counters of the in-GEMM row pull
+    int* done = nullptr;                // per-tile counters of the in-GEMM push
     int n_ready = 0;
+    __nv_bfloat16* stage = nullptr;     // [pairs, n_out] local output rows before the push
     cudaEvent_t ev[4] = {};             // optional step-phase timing events
     uint8_t* peer_base[kMaxRanks] = {};
     bool opened[kMaxRanks] = {};
@@ -369,7 +376,9 @@ extern "C" int ferret_ep_init(int rank, int world, int num_experts, int topk, in
     l = align_up(l + (size_t)pairs * nk * 4, 256);
     c->n_ready = (int)(pairs / 128 + c->El + 1);   // >= sum over experts of ceil(rows / 128)
     const size_t off_ready = l;
-    l = align_up(l + (size_t)c->n_ready * 4, 256);
+    l = align_up(l + (size_t)c->n_ready * 4 * 2, 256);     // ready, then done
+    const size_t off_stage = l;
+    l = align_up(l + (size_t)pairs * c->n_out * 2, 256);
 
     if (cudaMalloc(&c->sym, c->sym_bytes) != cudaSuccess || cudaMalloc(&c->loc, l) != cudaSuccess ||
         cudaMemset(c->sym, 0, c->sym_bytes) != cudaSuccess ||
@@ -388,6 +397,8 @@ extern "C" int ferret_ep_init(int rank, int world, int num_experts, int topk, in
     c->a = c->loc + off_a;
     c->a_s = reinterpret_cast<float*>(c->loc + off_as);
     c->ready = reinterpret_cast<int*>(c->loc + off_ready);
+    c->done = c->ready + c->n_ready;
+    c->stage = reinterpret_cast<__nv_bfloat16*>(c->loc + off_stage);
     cudaIpcMemHandle_t h;
     if (cudaMemcpy(c->remap, remap.data(), remap.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaIpcGetMemHandle(&h, c->sym) != cudaSuccess) {
@@ -506,6 +517,7 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
     d.epoch = c->epoch;
     d.failed = reinterpret_cast<int*>(c->epoch + 1);
     d.ready = c->ready;
+    d.done = c->done;
     d.n_ready = c->n_ready;
     const DevCtl ctl = make_ctl(info);
     // the prefill kernel pulls its rows itself (own = the rows one rank receives
@@ -548,10 +560,13 @@ extern "C" int ferret_ep_w13_forward(ferret_ep* c, const void* hidden_bf16, cons
         om.s_peers = reinterpret_cast<const float* const*>(c->tables + 3 * kMaxRanks);
         om.gather_topk = c->topk;
         om.ready = c->ready;
+        om.done = c->done;
     }
     if ((rc = record_event(c->ev[1], s)) != FERRET_OK) return rc;
-    rc = run_fp8_gemm(info, c->a, c->a_s, w_fp8, w_scale, my + c->off_out, c->offsets, 0, pairs,
-                      c->N, c->K, c->El, c->flags, own, s, om);
+    // (with the in-GEMM movers, `out` is the local staging matrix)
+    rc = run_fp8_gemm(info, c->a, c->a_s, w_fp8, w_scale,
+                      pull_in_gemm ? static_cast<void*>(c->stage) : static_cast<void*>(my + c->off_out),
+                      c->offsets, 0, pairs, c->N, c->K, c->El, c->flags, own, s, om);
     if (rc != FERRET_OK) return rc;
     if ((rc = record_event(c->ev[2], s)) != FERRET_OK) return rc;
     // 6. every rank's rows have landed

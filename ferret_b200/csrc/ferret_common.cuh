@@ -519,6 +519,18 @@ __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Warpgroup register reallocation (all threads of the warpgroup execute it):
+// lower this warpgroup's per-thread register count, or raise it from the
+// registers other warpgroups released.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -107,23 +107,22 @@ constexpr int kPfEpi = 256;
 constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
 constexpr int kPfMaxStages = 6;
 
-// Per epilogue warp: a 32-row x 32-column bf16 staging block (rows padded to
-// 80 bytes: conflict-free 16-byte writes) and the 32 rows' output pointers.
-constexpr int kPfStgRow = 80;
-constexpr int kPfStgWarp = 32 * kPfStgRow + 32 * 8;
+// The expert-parallel form adds six warps (warps 2-3 and a fourth warpgroup,
+// warps 12-15; the epilogue moves to warps 4-11): four pull the tile rows
+// from the peers and two push finished rows to them while the tile pipeline
+// runs.
+constexpr int kPfPullWarps = 4, kPfPushWarps = 2;
+constexpr int kPfPeerThreads = 16 * 32;
 
-// The staged-store (peer output) form adds warps that pull the tile rows from
-// the peers while the tile pipeline runs (expert parallelism).
-constexpr int kPfGatherWarps = 2;
-constexpr int kPfPeerThreads = kPfThreads + 32 * kPfGatherWarps;
-
-enum : int { SITE_ROWS = 11 };   // waiting for pulled rows to land
+// waits for pulled rows to land / for a tile's rows to be stored before the push
+enum : int { SITE_ROWS = 11, SITE_PUSH = 12 };
 
 struct PfLayout {
-    int stages_off, segs_off, segc_off, mts_off, part_off, stg_off, bar_off, misc_off, total;
+    int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
+// ep: the expert-parallel form (more threads for the block scan's scratch)
+__host__ __device__ inline PfLayout pf_layout(int stages, int E, bool ep) {
     PfLayout L;
     int o = 0;
     L.stages_off = o;
@@ -135,14 +134,8 @@ __host__ __device__ inline PfLayout pf_layout(int stages, int E, bool staged) {
     L.mts_off = o;
     o += 4 * (E + 1);
     L.part_off = o;
-    o += 4 * ((staged ? kPfPeerThreads : kPfThreads) + 1);
+    o += 4 * ((ep ? kPfPeerThreads : kPfThreads) + 1);
     o = (o + 7) & ~7;
-    L.stg_off = o;
-    if (staged) {
-        o = (o + 15) & ~15;
-        L.stg_off = o;
-        o += kPfStgWarp * (kPfEpi / 32);
-    }
     L.bar_off = o;
     o += 8 * (2 * kPfMaxStages + 2 * 2 + 2);
     L.misc_off = o;
@@ -261,8 +254,9 @@ int launch_fp8_decode(int nt, bool pair, const DeviceInfo* info, const void* a, 
 int launch_derive_segments(const DeviceInfo* info, const int32_t* m_indices, int M, int E,
                            int32_t* seg, int* cnt, int ncnt, cudaStream_t stream);
 
-// Prefill kernel (128 token rows x 256 weight rows per tile); peer outputs in om
-// select its staged-store form, which can also pull its A rows from the peers.
+// Prefill kernel (128 token rows x 256 weight rows per tile); om.gather selects
+// its expert-parallel form, which pulls its A rows from and pushes its output
+// rows to the peers itself.
 int launch_fp8_prefill(bool pair, const DeviceInfo* info, const void* a, const float* a_scale,
                        const void* w, const float* w_scale, void* out, const int32_t* seg,
                        int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,

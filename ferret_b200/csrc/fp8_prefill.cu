@@ -1,25 +1,171 @@
 // fp8_prefill.cu -- the prefill-shaped FP8 grouped GEMM (tokens on the MMA M
-// axis, 128 x 256 tiles), its staged-store form for outputs on other GPUs
-// (expert parallelism), and the opt-in CTA-pair form.
+// axis, 128 x 256 tiles), its expert-parallel form (token rows pulled from
+// and results pushed to the other GPUs by extra warps of the same kernel,
+// while the tiles run), and the opt-in CTA-pair form.
 #include "fp8_gemm_common.cuh"
 
 namespace ferret {
 namespace {
 
+// Expert-parallel form of the prefill kernel.  Extra warps move the rows
+// while the tiles run:
+//   * four pull warps per CTA copy the routed token rows (e4m3 + 1x128 scales) out of
+//     the source ranks' memory into the A operand, in tile order, with plain
+//     16-byte peer loads (NVLink), counting each landed row on its 128-row
+//     tile's `ready` counter (release).  The TMA producer waits for a tile's
+//     count before its first A load (acquire, then a proxy fence so the
+//     async-proxy loads see the rows); the epilogue waits the same way before
+//     reading the rows' scales.
+//   * the epilogue stores each tile into a local staging matrix, exactly as
+//     the single-GPU kernel stores its output, and each epilogue warp counts
+//     its part of the tile on the tile's `done` counter; the push warp, once
+//     every epilogue warp of every 256-column block of a 128-row tile has
+//     counted, two push warps per CTA copy those rows to their destination (row sorted[i] % own of
+//     rank sorted[i] / own) as whole contiguous rows: 8 KB (4 KB with SiLU)
+//     NVLink writes.
+// Neither mover waits on anything but counters that the other roles raise
+// without waiting on the movers, so every count completes while all CTAs are
+// resident (one CTA per SM, grid = SMs); every wait is bounded all the same.
+struct EpMoveArgs {
+    const int32_t* src;                 // [rows] global pair index of each sorted row
+    const uint8_t* const* q_peers;      // [world] every rank's e4m3 token rows
+    const float* const* s_peers;        // [world] every rank's 1x128 scales
+    __nv_bfloat16* const* out_peers;    // [world] every rank's output rows, (token, slot) order
+    uint8_t* a;                         // the A operand: pulled row i is written here
+    float* a_s;                         // its scales
+    int* ready;                         // [128-row tiles] rows landed, zero at launch
+    int* done;                          // [128-row tiles] warp-tiles stored, zero at launch
+    int own;                            // pairs per rank (tokens * topk)
+    int topk;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy view (the acquire before it) before its
+// later async-proxy accesses (the TMA loads of the rows that were pulled).
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until counter *cnt reaches `want` (acquire).
+__device__ bool wait_count(const int* cnt, int want, volatile int* abort_flag, const DevCtl& ctl,
+                           int site) {
+    if (ld_acquire_gpu(cnt) >= want) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        __nanosleep(128);
+        if (ld_acquire_gpu(cnt) >= want) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > ctl.timeout_ns) {
+            *abort_flag = 1;
+            report(ctl, DEV_TIMEOUT | (site << 8));
+            return false;
+        }
+    }
+}
+
+// Pull warp pw of this CTA: row slots blockIdx.x * kPfPullWarps + pw, then
+// every gridDim.x * kPfPullWarps-th, of the tile-ordered slot list (128 per
+// tile), so the rows land roughly in the order the tiles need them.
+__device__ __forceinline__ void ep_pull_rows(const EpMoveArgs& mv, int K, int E, const int* mt_start,
+                                             const int* seg_s, const int* seg_c, int pw, int lane) {
+    const int nk = K >> 7;
+    const int vec = K >> 4;                    // 16-byte words per row
+    const int slots = mt_start[E] * 128;
+    for (int idx = blockIdx.x * kPfPullWarps + pw; idx < slots; idx += gridDim.x * kPfPullWarps) {
+        const int mt = idx >> 7, i = idx & 127;
+        int e, row0, rows, nb;
+        decode_tile<128>(mt, 1, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+        if (i >= rows) continue;
+        const int r = row0 + i;
+        const int src = __ldg(mv.src + r);
+        const int g = src / mv.own;
+        const int tok = (src - g * mv.own) / mv.topk;
+        const uint4* q = reinterpret_cast<const uint4*>(mv.q_peers[g] + (size_t)tok * K);
+        const float* sc = mv.s_peers[g] + (size_t)tok * nk;
+        uint4* dst = reinterpret_cast<uint4*>(mv.a + (size_t)r * K);
+        // all of a lane's loads for a 4 KB piece of the row before its
+        // stores: one NVLink latency per piece
+        for (int base = 0; base < vec; base += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) v[j] = __ldcv(q + c);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) dst[c] = v[j];
+            }
+        }
+        for (int c = lane; c < nk; c += 32) mv.a_s[(size_t)r * nk + c] = __ldcv(sc + c);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_gpu_add(mv.ready + mt, 1);
+    }
+}
+
+// Push warp pw of this CTA: the same kind of slot walk; a row moves once
+// every epilogue warp of every 256-column block of its tile has counted.
+__device__ __forceinline__ void ep_push_rows(const EpMoveArgs& mv, const __nv_bfloat16* stage,
+                                             int ldo, int nbc, int E, const int* mt_start,
+                                             const int* seg_s, const int* seg_c, int pw, int lane,
+                                             volatile int* abort_flag, const DevCtl& ctl) {
+    const int vec = ldo >> 3;                  // 16-byte words per output row
+    const int slots = mt_start[E] * 128;
+    const int want = nbc * (kPfEpi / 32);
+    for (int idx = blockIdx.x * kPfPushWarps + pw; idx < slots; idx += gridDim.x * kPfPushWarps) {
+        const int mt = idx >> 7, i = idx & 127;
+        int e, row0, rows, nb;
+        decode_tile<128>(mt, 1, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+        if (i >= rows) continue;
+        if (!__all_sync(0xffffffffu, wait_count(mv.done + mt, want, abort_flag, ctl, SITE_PUSH)))
+            return;
+        const int r = row0 + i;
+        const int src = __ldg(mv.src + r);
+        const int g = src / mv.own;
+        const uint4* sp = reinterpret_cast<const uint4*>(stage + (size_t)r * ldo);
+        uint4* d = reinterpret_cast<uint4*>(mv.out_peers[g] + (size_t)(src - g * mv.own) * ldo);
+        for (int base = 0; base < vec; base += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) v[j] = __ldcg(sp + c);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = base + lane + 32 * j;
+                if (c < vec) d[c] = v[j];
+            }
+        }
+    }
+}
+
+// The tile pipeline of the prefill kernel and of its expert-parallel form.
 // REM: only the rows of each expert past its whole 256-row chunks (which the
 // CTA-pair kernel below takes), i.e. its last count % 256 rows.
-template <bool PAIR, bool REM = false>
-__global__ void __launch_bounds__(kPfThreads, 1)
-    fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
-                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
-    pdl_begin();
+// EP: the expert-parallel form (EpMoveArgs), kPfPeerThreads threads.
+template <bool PAIR, bool REM, bool EP>
+__device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUtensorMap* tm_a,
+                                             const GemmArgs& args, const EpMoveArgs& mv) {
+    constexpr int kNT = EP ? kPfPeerThreads : kPfThreads;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7;
     const int nbc = N >> 8;                        // 256-row weight tiles
-    const PfLayout L = pf_layout(NS, E, false);
+    const PfLayout L = pf_layout(NS, E, EP);
     int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
     int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
@@ -54,7 +200,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tmem_relinquish();
     }
     bool seg_bad = false;
-    for (int e = tid; e < E; e += kPfThreads) {
+    for (int e = tid; e < E; e += kNT) {
         int s, c;
         if (args.seg_pairs) {
             s = args.seg[2 * e];
@@ -84,12 +230,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int total = mt_start[E] * nbc;
+    constexpr int kEpi0 = EP ? 4 : 2;      // first epilogue warp
 
-    if (warp == 0) {
+    auto producer = [&]() {
         // ================= TMA producer =================
         if (elect_one()) {
-            tma_prefetch_desc(&tm_w);
-            tma_prefetch_desc(&tm_a);
+            tma_prefetch_desc(tm_w);
+            tma_prefetch_desc(tm_a);
             const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
             const uint64_t pol_a = policy_evict_last();
             int it = 0;
@@ -100,6 +247,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
                 const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
                 const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
+                if constexpr (EP) {
+                    // the tile's A rows are pulled by this kernel's own mover warp
+                    if (!wait_count(mv.ready + t / nbc, rows, abort_flag, args.ctl, SITE_ROWS)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_proxy_async_global();
+                }
                 for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
                     const int s = rp.slot;
                     if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
@@ -108,15 +263,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     const uint32_t dst = stage_base + s * kPfStage;
                     mbar_expect_tx(full_bar(s), kPfStage);
-                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
-                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
-                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst, tm_a, kb * 128, row0, full_bar(s), pol_a);
+                    tma_load_2d_hint(dst + 16384, tm_w, kb * 128, w0, full_bar(s), pol_w);
+                    tma_load_2d_hint(dst + 32768, tm_w, kb * 128, w1, full_bar(s), pol_w);
                 }
             }
             for (int i = max(0, it - NS); i < it; ++i)
                 mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
         }
-    } else if (warp == 1) {
+    };
+    auto mma_issuer = [&]() {
         // ================= MMA issuer =================
         if (elect_one()) {
             constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
@@ -144,9 +300,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_commit(drain_bar);
             mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
         }
-    } else {
+    };
+    auto epilogue = [&]() {
         // ================= epilogue: promotion + store =================
-        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int h = (warp - kEpi0) >> 2;       // column half: [64h, 64h+64) of each block
         const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
@@ -155,6 +312,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int e, row0, rows, nb;
             decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+            if constexpr (EP) {
+                // the rows' scales come from this kernel's own pull
+                if (!__all_sync(0xffffffffu, wait_count(mv.ready + t / nbc, rows, abort_flag,
+                                                        args.ctl, SITE_ROWS)))
+                    break;
+            }
             const bool live = r < rows;
             const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
             const int blk0 = PAIR ? nb : 2 * nb;
@@ -169,7 +332,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             bool ok = true;
             for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
-                const float sa = live ? __ldg(as_row + kb) : 0.0f;
+                // EP: a plain (L1-caching) load, ordered after the pull by the
+                // acquire above (the read-only path would not be)
+                const float sa = live ? (EP ? __ldca(as_row + kb) : __ldg(as_row + kb)) : 0.0f;
                 const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
                 ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
                                                        args.ctl, SITE_TFULL));
@@ -234,359 +399,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                 }
             }
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 1) {
-        __syncwarp();
-        tmem_dealloc(tmem_base, 512);
-    }
-}
-
-// Rows the staged kernel below pulls from the peers itself (expert
-// parallelism; OutMap describes the mapping).  A kernel argument of its own,
-// like SplitArgs, so the tile kernels' argument struct stays as measured.
-struct GatherArgs {
-    const int32_t* src;                 // [rows] global pair index per sorted row; nullptr: no pull
-    const uint8_t* const* q_peers;      // [world] every rank's e4m3 token rows
-    const float* const* s_peers;        // [world] every rank's 1x128 scales
-    uint8_t* a;                         // the A operand: row i is written here
-    float* a_s;                         // its scales
-    int* ready;                         // [128-row tiles] rows landed, zero at launch
-    int own;                            // pairs per rank (tokens * topk)
-    int topk;
-};
-
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
-    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Orders this thread's generic-proxy view (the acquire above) before its
-// later async-proxy accesses (the TMA loads of the rows that were pulled).
-__device__ __forceinline__ void fence_proxy_async_global() {
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// Bounded wait until tile counter *cnt reaches `want` rows (acquire).
-__device__ bool wait_rows(const int* cnt, int want, volatile int* abort_flag, const DevCtl& ctl) {
-    if (ld_acquire_gpu(cnt) >= want) return true;
-    const uint64_t t0 = global_ns();
-    for (;;) {
-        __nanosleep(128);
-        if (ld_acquire_gpu(cnt) >= want) return true;
-        if (*abort_flag) return false;
-        if (global_ns() - t0 > ctl.timeout_ns) {
-            *abort_flag = 1;
-            report(ctl, DEV_TIMEOUT | (SITE_ROWS << 8));
-            return false;
-        }
-    }
-}
-
-// The same kernel for output rows on other GPUs (expert parallelism): rows are
-// written through shared memory, 64 contiguous bytes of 8 rows per store
-// instruction, because 16-byte writes scattered over 32 rows make poor NVLink
-// transactions.  A separate function rather than a template switch of the one
-// above, so that the local kernel's code generation stays as measured.
-//
-// With GatherArgs.src set it also moves the token rows: kPfGatherWarps extra
-// warps per CTA copy the routed rows out of the source ranks' memory (plain
-// 16-byte peer loads, NVLink) into the A operand, in tile order, each landed
-// row counted on its tile's counter (release).  Before the first TMA load of
-// a tile's A rows the producer waits for that count (acquire, then a proxy
-// fence so the async-proxy TMA sees the rows); the epilogue waits the same way
-// before reading the rows' scales.  The pull of later tiles thus runs under
-// the MMAs of earlier ones instead of as a separate kernel before the GEMM.
-// The copy warps wait on nothing, so every count completes while all CTAs are
-// resident (one CTA per SM, grid = SMs); each wait is bounded all the same.
-template <bool PAIR>
-__global__ void __launch_bounds__(kPfPeerThreads, 1)
-    fp8_w13_prefill_peer_kernel(const __grid_constant__ CUtensorMap tm_w,
-                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
-                           const GatherArgs ga) {
-    pdl_begin();
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
-    const int nk = K >> 7;
-    const int nbc = N >> 8;                        // 256-row weight tiles
-    const PfLayout L = pf_layout(NS, E, true);
-    int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
-    int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
-    int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
-    int* part = reinterpret_cast<int*>(smem + L.part_off);
-    const uint32_t bar0 = smem_addr(smem + L.bar_off);
-    auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (kPfMaxStages + s); };
-    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
-    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
-    const uint32_t epi_bar = drain_bar + 8u;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
-    const uint32_t stage_base = smem_addr(smem + L.stages_off);
-
-    if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 1);
-        }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), kPfEpi);
-        }
-        mbar_init(drain_bar, 1);
-        mbar_init(epi_bar, kPfEpi);
-        *abort_flag = 0;
-        mbar_init_fence();
-    }
-    if (warp == 1) {
-        tmem_alloc(smem_addr(tmem_slot), 512);
-        tmem_relinquish();
-    }
-    bool seg_bad = false;
-    for (int e = tid; e < E; e += kPfPeerThreads) {
-        int s, c;
-        if (args.seg_pairs) {
-            s = args.seg[2 * e];
-            c = args.seg[2 * e + 1];
-        } else {
-            s = args.seg[e];
-            c = args.seg[e + 1] - s;
-        }
-        if (s < 0 || s > M || c < 0 || c > M - s) {
-            seg_bad = true;
-            s = min(max(s, 0), M);
-            c = min(max(c, 0), M - s);
-        }
-        seg_s[e] = s;
-        seg_c[e] = c;
-        mt_start[e] = (c + 127) >> 7;
-    }
-    if (seg_bad) report(args.ctl, DEV_LAYOUT);
-    __syncthreads();
-    block_exclusive_scan(mt_start, E, part);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-    const int total = mt_start[E] * nbc;
-
-    if (warp == 0) {
-        // ================= TMA producer =================
-        if (elect_one()) {
-            tma_prefetch_desc(&tm_w);
-            tma_prefetch_desc(&tm_a);
-            const uint64_t pol_w = policy_evict_last();     // reused by the expert's token tiles
-            const uint64_t pol_a = policy_evict_last();
-            int it = 0;
-            RingPos rp;
-            bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                int e, row0, rows, nb;
-                decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
-                const int w0 = PAIR ? e * N + nb * 128 : e * N + nb * 256;
-                const int w1 = PAIR ? e * N + (N >> 1) + nb * 128 : w0 + 128;
-                if (ga.src) {
-                    if (!wait_rows(ga.ready + t / nbc, rows, abort_flag, args.ctl)) {
-                        ok = false;
-                        break;
-                    }
-                    fence_proxy_async_global();
-                }
-                for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
-                    const int s = rp.slot;
-                    if (!mbar_wait(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl, SITE_EMPTY)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t dst = stage_base + s * kPfStage;
-                    mbar_expect_tx(full_bar(s), kPfStage);
-                    tma_load_2d_hint(dst, &tm_a, kb * 128, row0, full_bar(s), pol_a);
-                    tma_load_2d_hint(dst + 16384, &tm_w, kb * 128, w0, full_bar(s), pol_w);
-                    tma_load_2d_hint(dst + 32768, &tm_w, kb * 128, w1, full_bar(s), pol_w);
-                }
-            }
-            for (int i = max(0, it - NS); i < it; ++i)
-                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, SITE_DRAIN, false);
-        }
-    } else if (warp == 1) {
-        // ================= MMA issuer =================
-        if (elect_one()) {
-            constexpr uint32_t idesc = make_idesc(128, 256, 0, 0);
-            RingPos rs, ra;
-            bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
-                    const int s = rs.slot, a = ra.slot;
-                    if (!mbar_wait(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl, SITE_TEMPTY) ||
-                        !mbar_wait(full_bar(s), rs.phase, abort_flag, args.ctl, SITE_FULL)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t st = stage_base + s * kPfStage;
-                    const uint32_t d = tmem_base + a * 256;
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)
-                        mma_f8f6f4(d, sdesc_k_sw128(st + ks * 32), sdesc_k_sw128(st + 16384 + ks * 32),
-                                   idesc, ks > 0);
-                    tc_commit(empty_bar(s));
-                    tc_commit(tfull_bar(a));
-                }
-            }
-            tc_commit(drain_bar);
-            mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
-        }
-    } else if (warp >= kPfThreads / 32) {
-        // ================= row pull (expert parallelism) =================
-        if (ga.src) {
-            const int gw = warp - kPfThreads / 32;
-            const int nwarps = gridDim.x * kPfGatherWarps;
-            const int vec = K >> 4;                    // 16-byte words per row
-            const int slots = mt_start[E] * 128;       // 128 row slots per tile, in tile order
-            for (int idx = blockIdx.x * kPfGatherWarps + gw; idx < slots; idx += nwarps) {
-                const int mt = idx >> 7, i = idx & 127;
-                int e, row0, rows, nb;
-                decode_tile<128>(mt, 1, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
-                if (i >= rows) continue;
-                const int r = row0 + i;
-                const int src = __ldg(ga.src + r);
-                const int g = src / ga.own;
-                const int tok = (src - g * ga.own) / ga.topk;
-                const uint4* q = reinterpret_cast<const uint4*>(ga.q_peers[g] + (size_t)tok * K);
-                const float* sc = ga.s_peers[g] + (size_t)tok * nk;
-                uint4* dst = reinterpret_cast<uint4*>(ga.a + (size_t)r * K);
-                // all of a lane's loads for the row (16 words, 8 KB of the row
-                // per warp pass) before its stores: one NVLink latency per pass
-                for (int base = 0; base < vec; base += 32 * 16) {
-                    uint4 v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int c = base + lane + 32 * j;
-                        if (c < vec) v[j] = __ldcv(q + c);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int c = base + lane + 32 * j;
-                        if (c < vec) dst[c] = v[j];
-                    }
-                }
-                for (int c = lane; c < nk; c += 32) ga.a_s[(size_t)r * nk + c] = __ldcv(sc + c);
+            if constexpr (EP) {
+                // this warp's rows of the tile are stored: count it for the push
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) red_release_gpu_add(ga.ready + mt, 1);
+                if (lane == 0) red_release_gpu_add(mv.done + t / nbc, 1);
             }
+        }
+    };
+
+    if constexpr (EP) {
+        // Warpgroups 0 (TMA, MMA, pull, push) and 3 (pull x3, push) hand
+        // registers to the two epilogue warpgroups (1, 2), which then hold their
+        // accumulators without spilling: launched at 128 per thread, 2 x 128 x 64
+        // + 2 x 128 x 192 = 512 x 128, and per SM sub-partition
+        // 32 x (64 + 64 + 192 + 192) = 16384.
+        if (warp < 4 || warp >= 12) {
+            setmaxnreg_dec<64>();
+            if (warp == 0) producer();
+            else if (warp == 1) mma_issuer();
+            else if (warp == 2 || warp >= 13)
+                ep_pull_rows(mv, K, E, mt_start, seg_s, seg_c, warp == 2 ? 0 : warp - 12, lane);
+            else
+                ep_push_rows(mv, args.out, PAIR ? (N >> 1) : N, nbc, E, mt_start, seg_s, seg_c,
+                             warp == 3 ? 0 : 1, lane, abort_flag, args.ctl);
+        } else {
+            setmaxnreg_inc<192>();
+            epilogue();
         }
     } else {
-        // ================= epilogue: promotion + store =================
-        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
-        const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
-        const int r = q * 32 + lane;
-        const int ldo = PAIR ? (N >> 1) : N;
-        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-        uint8_t* stg = smem + L.stg_off + (warp - 2) * kPfStgWarp;
-        __nv_bfloat16** rowp = reinterpret_cast<__nv_bfloat16**>(stg + 32 * kPfStgRow);
-        RingPos ra;
-        for (int t = blockIdx.x; t < total; t += gridDim.x) {
-            int e, row0, rows, nb;
-            decode_tile<128>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
-            if (ga.src && !__all_sync(0xffffffffu,
-                                      wait_rows(ga.ready + t / nbc, rows, abort_flag, args.ctl)))
-                break;
-            const bool live = r < rows;
-            const float* as_row = args.a_scale + (size_t)(row0 + (live ? r : 0)) * nk;
-            const int blk0 = PAIR ? nb : 2 * nb;
-            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
-            const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
-            const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
-            float acc0[64], acc1[64];
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                acc0[j] = 0.0f;
-                acc1[j] = 0.0f;
-            }
-            bool ok = true;
-            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
-                const float sa = live ? __ldcg(as_row + kb) : 0.0f;
-                const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
-                ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(ra.slot), ra.phase, abort_flag,
-                                                       args.ctl, SITE_TFULL));
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
-#pragma unroll
-                for (int c = 0; c < 64; c += 16) {
-                    float v[16], u[16];
-                    tmem_ld16(tb + c, v);
-                    tmem_ld16(tb + 128 + c, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
-                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
-                    }
-                }
-                tc_fence_before();
-                mbar_arrive(tempty_bar(ra.slot));
-            }
-            if (!ok) break;
-            int orow = row0 + r;
-            if (live && args.out_rows) {
-                orow = __ldg(args.out_rows + row0 + r);
-                if (orow < 0 || orow >= args.out_total) orow = -1;
-            }
-            // Staged: every store instruction writes 64 contiguous bytes of 8
-            // rows instead of 16 bytes of 32 rows.
-            rowp[lane] = (live && orow >= 0) ? out_row_ptr(args, orow, ldo) : nullptr;
-#pragma unroll
-            for (int k = 0; k < (PAIR ? 2 : 4); ++k) {
-                // chunk k: 32 columns of this thread's row
-                uint4 pk[4];
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    uint32_t* pw = reinterpret_cast<uint32_t*>(&pk[v]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int c = (PAIR ? k * 32 : (k & 1) * 32) + v * 8 + 2 * j;
-                        __nv_bfloat162 b;
-                        if (PAIR)
-                            b = __floats2bfloat162_rn(silu_mul(acc0[c], acc1[c]),
-                                                      silu_mul(acc0[c + 1], acc1[c + 1]));
-                        else if (k < 2)
-                            b = __floats2bfloat162_rn(acc0[c], acc0[c + 1]);
-                        else
-                            b = __floats2bfloat162_rn(acc1[c], acc1[c + 1]);
-                        pw[j] = *reinterpret_cast<const uint32_t*>(&b);
-                    }
-                }
-                uint4* srow = reinterpret_cast<uint4*>(stg + lane * kPfStgRow);
-#pragma unroll
-                for (int v = 0; v < 4; ++v) srow[v] = pk[v];
-                __syncwarp();
-                const int col = PAIR ? nb * 128 + h * 64 + k * 32
-                                     : nb * 256 + (k >> 1) * 128 + h * 64 + (k & 1) * 32;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int idx = i * 32 + lane, row = idx >> 2, part = idx & 3;
-                    __nv_bfloat16* o = rowp[row];
-                    if (o)
-                        reinterpret_cast<uint4*>(o + col)[part] =
-                            *reinterpret_cast<const uint4*>(stg + row * kPfStgRow + part * 16);
-                }
-                __syncwarp();
-            }
-        }
+        if (warp == 0) producer();
+        else if (warp == 1) mma_issuer();
+        else epilogue();
     }
 
     tc_fence_before();
@@ -596,6 +440,24 @@ __global__ void __launch_bounds__(kPfPeerThreads, 1)
         __syncwarp();
         tmem_dealloc(tmem_base, 512);
     }
+}
+
+
+template <bool PAIR, bool REM = false>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
+    pdl_begin();
+    prefill_body<PAIR, REM, false>(&tm_w, &tm_a, args, EpMoveArgs{});
+}
+
+template <bool PAIR>
+__global__ void __launch_bounds__(kPfPeerThreads, 1)
+    fp8_w13_prefill_ep_kernel(const __grid_constant__ CUtensorMap tm_w,
+                              const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
+                              const EpMoveArgs mv) {
+    pdl_begin();
+    prefill_body<PAIR, false, true>(&tm_w, &tm_a, args, mv);
 }
 
 // ---------------------------------------------------------------------------
@@ -935,10 +797,10 @@ int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const floa
 }
 
 
-template <bool PAIR, bool STAGED>
+template <bool PAIR, bool EP>
 int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
-                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
-                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
+                         const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                         int N, int K, int E, cudaStream_t stream, const OutMap& om) {
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
                           128, true);
@@ -946,14 +808,14 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
     if (rc != FERRET_OK) return rc;
     const int budget = info->max_smem_optin - 1024;
-    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E, STAGED).total) / kPfStage);
+    const int stages = std::min(kPfMaxStages, (budget - pf_layout(0, E, EP).total) / kPfStage);
     if (stages < 2) return FERRET_ERR_SHAPE;
-    const int smem = pf_layout(stages, E, STAGED).total + 1024;
+    const int smem = pf_layout(stages, E, EP).total + 1024;
     auto kern_local = fp8_w13_prefill_kernel<PAIR>;
-    auto kern_peer = fp8_w13_prefill_peer_kernel<PAIR>;
+    auto kern_ep = fp8_w13_prefill_ep_kernel<PAIR>;
     const cudaError_t ae =
-        STAGED ? cudaFuncSetAttribute(kern_peer, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-               : cudaFuncSetAttribute(kern_local, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        EP ? cudaFuncSetAttribute(kern_ep, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+           : cudaFuncSetAttribute(kern_local, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (ae != cudaSuccess) {
         cudaGetLastError();
         return FERRET_ERR_CUDA;
@@ -964,9 +826,9 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.seg = seg;
     g.seg_pairs = seg_pairs;
     g.out = static_cast<__nv_bfloat16*>(out);
-    g.out_rows = om.rows;
+    g.out_rows = EP ? nullptr : om.rows;     // EP: tiles go to the local staging rows
     g.out_total = om.total;
-    g.out_peers = om.peers;
+    g.out_peers = EP ? nullptr : om.peers;
     g.peer_rows = om.peer_rows;
     g.M = M;
     g.N = N;
@@ -974,34 +836,34 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.E = E;
     g.stages = stages;
     g.ctl = make_ctl(info);
-    if (!STAGED) return launch_kernel(kern_local, dim3(info->num_sms), dim3(kPfThreads), smem, stream,
-                                      tm_w, tm_a, g);
-    GatherArgs ga = {};
-    if (om.gather) {
-        if (!om.rows || !om.q_peers || !om.s_peers || !om.ready || om.peer_rows <= 0 ||
-            om.gather_topk <= 0)
-            return FERRET_ERR_NULL;
-        ga.src = om.rows;
-        ga.q_peers = om.q_peers;
-        ga.s_peers = om.s_peers;
-        ga.a = static_cast<uint8_t*>(const_cast<void*>(a));
-        ga.a_s = const_cast<float*>(a_scale);
-        ga.ready = om.ready;
-        ga.own = om.peer_rows;
-        ga.topk = om.gather_topk;
-    }
-    return launch_kernel(kern_peer, dim3(info->num_sms), dim3(kPfPeerThreads), smem, stream, tm_w,
-                         tm_a, g, ga);
+    if (!EP) return launch_kernel(kern_local, dim3(info->num_sms), dim3(kPfThreads), smem, stream,
+                                  tm_w, tm_a, g);
+    if (!om.rows || !om.peers || !om.q_peers || !om.s_peers || !om.ready || !om.done ||
+        om.peer_rows <= 0 || om.gather_topk <= 0)
+        return FERRET_ERR_NULL;
+    EpMoveArgs mv;
+    mv.src = om.rows;
+    mv.q_peers = om.q_peers;
+    mv.s_peers = om.s_peers;
+    mv.out_peers = om.peers;
+    mv.a = static_cast<uint8_t*>(const_cast<void*>(a));
+    mv.a_s = const_cast<float*>(a_scale);
+    mv.ready = om.ready;
+    mv.done = om.done;
+    mv.own = om.peer_rows;
+    mv.topk = om.gather_topk;
+    return launch_kernel(kern_ep, dim3(info->num_sms), dim3(kPfPeerThreads), smem, stream, tm_w,
+                         tm_a, g, mv);
 }
 
 template <bool PAIR>
 int launch_fp8_prefill_p(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
-                       const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
-                       int N, int K, int E, cudaStream_t stream, const OutMap& om = OutMap{}) {
-    return om.peers ? launch_fp8_prefill_t<PAIR, true>(info, a, a_scale, w, w_scale, out, seg,
-                                                       seg_pairs, M, N, K, E, stream, om)
-                    : launch_fp8_prefill_t<PAIR, false>(info, a, a_scale, w, w_scale, out, seg,
-                                                        seg_pairs, M, N, K, E, stream, om);
+                         const float* w_scale, void* out, const int32_t* seg, int seg_pairs, int M,
+                         int N, int K, int E, cudaStream_t stream, const OutMap& om) {
+    return om.gather ? launch_fp8_prefill_t<PAIR, true>(info, a, a_scale, w, w_scale, out, seg,
+                                                        seg_pairs, M, N, K, E, stream, om)
+                     : launch_fp8_prefill_t<PAIR, false>(info, a, a_scale, w, w_scale, out, seg,
+                                                         seg_pairs, M, N, K, E, stream, om);
 }
 
 }  // namespace
