@@ -38,6 +38,7 @@ SIGNATURES = {
     "ferret_moe_align_block_size": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "ferret_quant_act_fp8_1x128": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_quant_act_fp8_1x128_ue8m0": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+    "ferret_quant_act_fp8_1x128_scatter": (_i, [_p, _i, _i, _p, _p, _i, _i, _p, _p, _p, _i, _p]),
     "ferret_fp8_gather_rows": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p]),
     "ferret_fp8_grouped_gemm_nt_contiguous": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _sz, _p]),

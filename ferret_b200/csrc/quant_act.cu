@@ -29,7 +29,11 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 // latency of the gathered row reads, not by HBM, at decode sizes).
 // UE8M0: the scale is the smallest power of two >= fl(amax / 448), taken from
 // the fp32 bits (exact; no log2), and x is multiplied by its exact inverse.
-template <bool UE8M0>
+// SCATTER: row r is token r (R = x_rows), and its quantized row is written to
+// every row inv[r * gather_div + j], j < gather_div, that is not negative (the
+// expert-sorted positions of the token's top-k pairs): each token is
+// quantized once and its bytes go straight to its routed copies.
+template <bool UE8M0, bool SCATTER = false>
 __global__ void __launch_bounds__(kQuantThreads)
     quant_act_kernel(const __nv_bfloat16* __restrict__ x, int x_rows,
                      const int32_t* __restrict__ gather, int gather_div, int R, int K,
@@ -46,7 +50,7 @@ __global__ void __launch_bounds__(kQuantThreads)
         const int r = (int)(task / tasks_per_row);
         const int b0 = (int)(task - (long long)r * tasks_per_row) * kBlocksPerTask;
         long long src = r;
-        if (gather) {
+        if (!SCATTER && gather) {
             const int g = gather[r];
             src = g < 0 ? -1 : g / gather_div;
             if (src >= x_rows) {            // out-of-range gather: zero row + status
@@ -103,6 +107,16 @@ __global__ void __launch_bounds__(kQuantThreads)
                     __NV_SATFINITE, __NV_E4M3);
                 packed[j] = (uint32_t)lo | ((uint32_t)hi << 16);
             }
+            if (SCATTER) {
+                for (int j = 0; j < gather_div; ++j) {
+                    const int p = __ldg(gather + (long long)r * gather_div + j);
+                    if (p < 0) continue;
+                    *reinterpret_cast<uint2*>(q + (long long)p * K + b * 128 + hl * 8) =
+                        make_uint2(packed[0], packed[1]);
+                    if (hl == 0) scale[(long long)p * nk + b] = sc;
+                }
+                continue;
+            }
             uint8_t* qdst = q + (long long)r * K + b * 128 + hl * 8;
             if (src < 0) {
                 packed[0] = packed[1] = 0u;
@@ -151,6 +165,76 @@ extern "C" int ferret_quant_act_fp8_1x128_ue8m0(const void* x_bf16, int x_rows,
                                                 const int32_t* gather_rows, int gather_div, int R,
                                                 int K, void* a_fp8, float* a_scale, void* stream) {
     return quant_act<true>(x_bf16, x_rows, gather_rows, gather_div, R, K, a_fp8, a_scale, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Quantize-and-scatter: each token row is quantized once and written to the
+// expert-sorted positions of its top-k pairs (the inverse of the permutation's
+// sorted_rows), which gives the same A operand as the gathered quantizer with
+// topk-fold less arithmetic and without a separate row-gather pass.
+// ---------------------------------------------------------------------------
+namespace ferret {
+namespace {
+
+// inv[sorted[p]] = p for the valid sorted positions p < offsets[E]
+// (inv pre-filled with -1: pairs whose expert id is invalid keep -1).
+__global__ void __launch_bounds__(256)
+    inverse_rows_kernel(const int32_t* __restrict__ sorted, const int32_t* __restrict__ off_end,
+                        int R, int32_t* __restrict__ inv, DevCtl ctl) {
+    pdl_begin();
+    const int valid = *off_end;
+    for (int p = blockIdx.x * 256 + threadIdx.x; p < R; p += gridDim.x * 256) {
+        if (p >= valid) continue;
+        const int v = sorted[p];
+        if (v < 0 || v >= R) {
+            report(ctl, DEV_BAD_ROW);
+            continue;
+        }
+        inv[v] = p;
+    }
+}
+
+}  // namespace
+}  // namespace ferret
+
+extern "C" int ferret_quant_act_fp8_1x128_scatter(const void* x_bf16, int T, int topk,
+                                                  const int32_t* sorted_rows,
+                                                  const int32_t* expert_offsets, int E, int K,
+                                                  void* a_fp8, float* a_scale, int32_t* inv_ws,
+                                                  int flags, void* stream) {
+    if (T < 0 || topk <= 0 || E <= 0 || K <= 0 || (K % 128) != 0) return FERRET_ERR_SHAPE;
+    if ((long long)T * topk >= (1ll << 31)) return FERRET_ERR_SHAPE;
+    if (T == 0) return FERRET_OK;
+    if (!x_bf16 || !sorted_rows || !expert_offsets || !a_fp8 || !a_scale || !inv_ws)
+        return FERRET_ERR_NULL;
+    if ((reinterpret_cast<uintptr_t>(x_bf16) & 15u) || (reinterpret_cast<uintptr_t>(a_fp8) & 7u) ||
+        (reinterpret_cast<uintptr_t>(a_scale) & 3u) || (reinterpret_cast<uintptr_t>(inv_ws) & 3u))
+        return FERRET_ERR_ALIGN;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&info);
+    if (rc != FERRET_OK) return rc;
+    cudaStream_t s = as_stream(stream);
+    const int R = T * topk;
+    if (cudaMemsetAsync(inv_ws, 0xFF, (size_t)R * sizeof(int32_t), s) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    {
+        const int want = (R + 255) / 256;
+        const int grid = want < info->num_sms * 8 ? want : info->num_sms * 8;
+        if ((rc = launch_kernel(inverse_rows_kernel, dim3(grid), dim3(256), 0, s, sorted_rows,
+                                expert_offsets + E, R, inv_ws, make_ctl(info))) != FERRET_OK)
+            return rc;
+    }
+    const long long tasks = (long long)T * ((K / 128 + kBlocksPerTask - 1) / kBlocksPerTask);
+    const long long want = (tasks + (kQuantThreads / 32) - 1) / (kQuantThreads / 32);
+    const int grid = (int)(want < (long long)info->num_sms * 16 ? want : (long long)info->num_sms * 16);
+    const bool ue8m0 = (flags & FERRET_UE8M0_SCALES) != 0;
+    return launch_kernel(ue8m0 ? quant_act_kernel<true, true> : quant_act_kernel<false, true>,
+                         dim3(grid), dim3(kQuantThreads), 0, s,
+                         static_cast<const __nv_bfloat16*>(x_bf16), T,
+                         static_cast<const int32_t*>(inv_ws), topk, T, K,
+                         static_cast<uint8_t*>(a_fp8), a_scale, make_ctl(info));
 }
 
 // ---------------------------------------------------------------------------

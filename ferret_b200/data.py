@@ -60,8 +60,9 @@ CONFIGS = {
     # small FP8 prefill case for ncu captures (32 experts, 0.94 GB of weights)
     "dsv3_prefill_small": W13Config("dsv3_prefill_small", E=32, topk=8, T=2048, K=7168, N=4096,
                                     routing="zipf"),
-    # small INT4 case for ncu captures (~35 active experts, ~0.6 GB of weights > L2)
-    "kimi_int4_small": W13Config("kimi_int4_small", E=48, topk=8, T=8, K=7168, N=4096,
+    # small INT4 case for ncu captures (128 routed rows over ~70 active experts,
+    # ~1.1 GB of weights > L2; the decode kernel's regime, like configuration 4)
+    "kimi_int4_small": W13Config("kimi_int4_small", E=96, topk=8, T=16, K=7168, N=4096,
                                  quant="int4"),
 }
 

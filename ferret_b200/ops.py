@@ -121,6 +121,31 @@ def per_token_cast_to_fp8(x: torch.Tensor, gather_rows: torch.Tensor | None = No
     return q, s
 
 
+def per_token_cast_to_fp8_scatter(x: torch.Tensor, sorted_rows: torch.Tensor,
+                                  expert_offsets: torch.Tensor, topk: int, out=None,
+                                  use_ue8m0: bool = False):
+    """bf16 [T, K] -> (e4m3 [T*topk, K], f32 [T*topk, K/128]) in expert-sorted
+    order: row p holds token sorted_rows[p] // topk for p < expert_offsets[-1]
+    (later rows are left as allocated).  Each token is quantized once; same
+    bytes as per_token_cast_to_fp8(x, sorted_rows, topk) on those rows."""
+    _need(x, torch.bfloat16, "x", 2)
+    _need(sorted_rows, torch.int32, "sorted_rows", 1)
+    _need(expert_offsets, torch.int32, "expert_offsets", 1)
+    T, K = x.shape
+    R = T * topk
+    if out is None:
+        q = torch.empty(R, K, dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.empty(R, K // 128, dtype=torch.float32, device=x.device)
+    else:
+        q, s = out
+    inv = torch.empty(R, dtype=torch.int32, device=x.device)
+    check(lib().ferret_quant_act_fp8_1x128_scatter(
+        _ptr(x), T, topk, _ptr(sorted_rows), _ptr(expert_offsets), expert_offsets.numel() - 1, K,
+        _ptr(q), _ptr(s), _ptr(inv), FERRET_UE8M0_SCALES if use_ue8m0 else 0, _stream()),
+        "ferret_quant_act_fp8_1x128_scatter")
+    return q, s
+
+
 def m_grouped_fp8_gemm_nt_contiguous(a, b, out: torch.Tensor, m_indices: torch.Tensor | None,
                                      disable_ue8m0_cast: bool = True,
                                      expert_offsets: torch.Tensor | None = None,
@@ -198,8 +223,9 @@ def m_grouped_fp8_gemm_scatter(a, b, out: torch.Tensor, expert_offsets: torch.Te
         "ferret_fp8_grouped_gemm_scatter")
 
 
-# Routed rows above which the W13 path quantizes each token once and gathers
-# the FP8 copies (identical bytes; topk-fold less quantizer arithmetic).
+# Routed rows above which the W13 path quantizes each token once and scatters
+# its FP8 row to its routed copies (identical bytes; topk-fold less quantizer
+# arithmetic, and no separate row-gather pass).
 QUANT_ONCE_ROWS = 8192
 
 
@@ -219,8 +245,7 @@ class W13Buffers:
         self.perm_ws_bytes = ws
         self.quant_once = R > QUANT_ONCE_ROWS and topk > 1
         if self.quant_once:
-            self.q_tok = torch.empty(T, K, dtype=torch.uint8, device=device)
-            self.s_tok = torch.empty(T, K // 128, dtype=torch.float32, device=device)
+            self.inv = torch.empty(R, dtype=torch.int32, device=device)
 
 
 def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
@@ -257,11 +282,11 @@ def fp8_moe_w13(hidden: torch.Tensor, topk_ids: torch.Tensor, W: torch.Tensor,
     qname = "ferret_quant_act_fp8_1x128_ue8m0" if use_ue8m0 else "ferret_quant_act_fp8_1x128"
     quant = getattr(L, qname)
     if bufs.quant_once:
-        # each token once, then its topk routed copies in expert order
-        check(quant(_ptr(hidden), T, None, 1, T, K, _ptr(bufs.q_tok), _ptr(bufs.s_tok), s), qname)
-        check(L.ferret_fp8_gather_rows(_ptr(bufs.q_tok), _ptr(bufs.s_tok), T,
-                                       _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
-                                       _ptr(bufs.a_scale), s), "ferret_fp8_gather_rows")
+        # each token quantized once, written straight to its topk expert-sorted rows
+        check(L.ferret_quant_act_fp8_1x128_scatter(
+            _ptr(hidden), T, topk, _ptr(bufs.sorted_rows), _ptr(bufs.offsets), E, K, _ptr(bufs.a),
+            _ptr(bufs.a_scale), _ptr(bufs.inv), FERRET_UE8M0_SCALES if use_ue8m0 else 0, s),
+            "ferret_quant_act_fp8_1x128_scatter")
     else:
         check(quant(_ptr(hidden), T, _ptr(bufs.sorted_rows), topk, R, K, _ptr(bufs.a),
                     _ptr(bufs.a_scale), s), qname)

@@ -159,6 +159,28 @@ FERRET_API int ferret_quant_act_fp8_1x128_ue8m0(const void* x_bf16, int x_rows,
                                                 int K, void* a_fp8, float* a_scale, void* stream);
 
 /*
+ * Quantize-and-scatter form of the 1x128 activation quantizer (the A operand
+ * of the W13 grouped GEMM in one pass from the token-ordered hidden states):
+ * each token row of x_bf16 [T, K] is quantized once (the algorithm of
+ * ferret_quant_act_fp8_1x128, or of its UE8M0 form with flags =
+ * FERRET_UE8M0_SCALES) and written to the expert-sorted rows of its top-k
+ * pairs: row p of a_fp8 [T*topk, K] / a_scale [T*topk, K/128] gets token
+ * sorted_rows[p] / topk for every p < expert_offsets[E] (sorted_rows and
+ * expert_offsets [E+1] from ferret_moe_permute); rows from expert_offsets[E]
+ * on are not written.  Bit-identical to ferret_quant_act_fp8_1x128 with
+ * gather_rows = sorted_rows, gather_div = topk on those rows.
+ * inv_ws: int32 [T*topk] scratch (the inverse permutation), caller-owned.
+ * No reference counterpart as one call: it replaces per_token_cast_to_fp8
+ * (baselines/fp8-group-gemm/baseline_dsv3_decode.py:42) followed by the row
+ * order the grouped GEMM needs.  Limits: K % 128 == 0.
+ */
+FERRET_API int ferret_quant_act_fp8_1x128_scatter(const void* x_bf16, int T, int topk,
+                                                  const int32_t* sorted_rows,
+                                                  const int32_t* expert_offsets, int E, int K,
+                                                  void* a_fp8, float* a_scale, int32_t* inv_ws,
+                                                  int flags, void* stream);
+
+/*
  * Row gather of quantized rows (no reference counterpart; an alternative to
  * the gathered quantizer above with identical output): out row r = row
  * rows[r] / div of q_fp8 [src_rows, K] / q_scale [src_rows, K/128]

@@ -125,6 +125,30 @@ def test_quant_gather_bit_exact(ops):
     assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
 
 
+@pytest.mark.parametrize("ue8m0", [False, True])
+@pytest.mark.parametrize("T,topk,E,K", [(5, 3, 4, 256), (1024, 8, 256, 7168), (3000, 8, 64, 512)])
+def test_quant_scatter_equals_gathered_quant(ops, T, topk, E, K, ue8m0):
+    """Quantize-and-scatter (each token once, written to its top-k expert-sorted
+    rows) gives the gathered quantizer's bytes on every valid sorted row, also
+    with dropped pairs; rows past the valid ones are left alone."""
+    from ferret_b200 import data
+    x = data.activations(T, K, seed=T).cuda()
+    ids = data.routing(T, E, topk, "zipf").cuda()
+    ids[1, 0] = -1
+    ids[T - 1, topk - 1] = E + 3
+    rows, offs, _ = ops.moe_permute(ids, E)
+    R = int(offs[-1])
+    qg, sg = ops.per_token_cast_to_fp8(x, rows, topk, use_ue8m0=ue8m0)
+    qs = torch.full((T * topk, K), 0x55, dtype=torch.uint8, device="cuda")
+    ss = torch.full((T * topk, K // 128), -7.0, device="cuda")
+    ops.per_token_cast_to_fp8_scatter(x, rows, offs, topk, out=(qs, ss), use_ue8m0=ue8m0)
+    torch.cuda.synchronize()
+    assert torch.equal(qs[:R], qg.view(torch.uint8)[:R])
+    assert torch.equal(ss[:R], sg[:R])
+    assert (qs[R:] == 0x55).all() and (ss[R:] == -7.0).all()
+    assert ops.last_device_status() == 0
+
+
 @pytest.mark.parametrize("T,topk,K", [(5, 3, 256), (1024, 8, 7168)])
 def test_gather_rows_equals_gathered_quant(ops, T, topk, K):
     """Quantize-once + ferret_fp8_gather_rows gives the bytes of the gathered

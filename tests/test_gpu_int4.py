@@ -102,9 +102,10 @@ def test_int4_vs_oracle(ops, T, E, K, N, topk, silu, tile):
     (64, 384, 1024, 256, 8, False, False),
 ])
 def test_int4_decode_kernel_vs_oracle(ops, T, E, K, N, topk, silu, skew):
-    """The register-dequant decode kernel (chosen automatically when the routed
-    rows average at most 4 per possibly-active expert): all pairs against the
-    oracle, dropped pairs untouched, experts with more rows than one 8-row pass."""
+    """The INT4 call at decode shapes: the library takes the register-dequant
+    decode kernel for more than 64 routed rows averaging at most 4 per possible
+    expert (the last case), the tensor-core kernel otherwise; all pairs against
+    the oracle, dropped pairs untouched, experts with several 8-row passes."""
     h, rq, sc, ids = inputs(T * 5 + E, T, E, K, N, topk)
     ids = ids.copy()
     if skew:
