@@ -45,7 +45,8 @@ def test_roofline_picks_the_longer_bound():
 
 def test_traffic_figures_come_from_profiles():
     for tag in ("fp8_w13_grouped_dsv3_decode", "fp8_w13_prefill_dsv3_prefill",
-                "int4_w13_grouped_kimi_int4_decode"):
+                "int4_w13_grouped_kimi_int4_decode", "fp8_w13_prefill_ep_prefill",
+                "int4_w13_decode_kimi_int4_decode"):
         t = bench.read_traffic(tag)
         assert t is not None and t > 1e9, tag
     assert bench.read_traffic("no_such_kernel_workload") is None
