@@ -270,7 +270,7 @@ def run(args, cfg):
         slow = _max(float(rank) if gemm_ms >= t_gemm else -1.0, dev)
         pk = bench.peaks()
         prefill = (Tl * cfg.topk + El - 1) // El > 48 and cfg.N % 256 == 0
-        kname = "fp8_w13_prefill_peer_kernel" if prefill and mode == "p2p" else \
+        kname = "fp8_w13_prefill_ep_kernel" if prefill and mode == "p2p" else \
                 "fp8_w13_prefill_kernel" if prefill else "fp8_w13_grouped_kernel"
         rl = bench.roofline(byts, loc_flops, gemm_ms, pk, kname)
         rl_t = torch.tensor([rl["frac"], rl["achieved"], float(byts), loc_flops], dtype=torch.float64,
