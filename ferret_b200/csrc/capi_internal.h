@@ -112,6 +112,20 @@ inline int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t s
     return FERRET_OK;
 }
 
+// True when `kern` launches with at least `regs` registers per thread.  A
+// kernel whose warpgroups trade registers with setmaxnreg assumes the launch
+// total (threads x registers) its split adds up to; with fewer, an increase
+// could never be granted.
+template <typename... KArgs>
+inline bool kernel_has_regs(void (*kern)(KArgs...), int regs) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return fa.numRegs >= regs;
+}
+
 // The same for a kernel of CTA pairs (thread-block clusters of 2 along x).
 // grid.x must be even.
 template <typename... KArgs, typename... Args>

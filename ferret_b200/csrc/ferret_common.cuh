@@ -504,8 +504,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x N (16 or 32) columns -> N registers per thread.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[N]) {
+    static_assert(N == 16 || N == 32, "16 or 32 columns per load");
+    if constexpr (N == 16) tmem_ld16(taddr, v);
+    else tmem_ld32(taddr, v);
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// (a0, a1) = (v0, v1) * s + (a0, a1) in one packed fma.rn.f32x2: each lane is
+// a fused multiply-add rounded to nearest, exactly what fmaf gives, at half
+// the instruction count.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, float s) {
+    uint64_t a, v, ss;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(v0), "f"(v1));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(v), "l"(ss));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
 }
 
 // Programmatic dependent launch: every kernel of the library is launched

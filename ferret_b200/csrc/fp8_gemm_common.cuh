@@ -66,6 +66,71 @@ __device__ __forceinline__ __nv_bfloat16* out_row_ptr(const GemmArgs& a, int oro
     return a.out + (size_t)orow * ldo;
 }
 
+// One K block of the prefill epilogue: this thread's row of the 256-column
+// TMEM partial at `tb` (columns [c0, c0 + CPH) of each 128-column half, the
+// thread's column group) scaled into its accumulators, acc0 for the first
+// weight block (s0 = a_scale * w_scale[block 0]) and acc1 for the second (s1).
+// The caller waits for the partial (tfull) before and releases the buffer after.
+template <int CPH, int LD>
+__device__ __forceinline__ void promote_kblock(uint32_t tb, float (&acc0)[CPH], float (&acc1)[CPH],
+                                               float s0, float s1) {
+#pragma unroll
+    for (int c = 0; c < CPH; c += LD) {
+        float v[LD], u[LD];
+        tmem_ld_cols<LD>(tb + c, v);
+        tmem_ld_cols<LD>(tb + 128 + c, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < LD; j += 2) {
+            ffma2(acc0[c + j], acc0[c + j + 1], v[j], v[j + 1], s0);
+            ffma2(acc1[c + j], acc1[c + j + 1], u[j], u[j + 1], s1);
+        }
+    }
+}
+
+// Stores one row of a finished prefill tile: the thread's CPH columns of each
+// weight block, as bf16 (16-byte stores), at output row `o`, output tile nb,
+// column group h.  PAIR (SiLU): silu(gate) * up of the two blocks into 128
+// output columns per tile; otherwise both blocks side by side (256 columns).
+template <bool PAIR, int CPH>
+__device__ __forceinline__ void store_tile_row(__nv_bfloat16* o, int nb, int h,
+                                               const float (&acc0)[CPH], const float (&acc1)[CPH]) {
+    if (PAIR) {
+        uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * CPH);
+#pragma unroll
+        for (int c = 0; c < CPH; c += 8) {
+            uint4 pk;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __nv_bfloat162 b = __floats2bfloat162_rn(
+                    silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
+                    silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
+                pw[j] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            dst[c >> 3] = pk;
+        }
+    } else {
+        uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * CPH);
+        uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * CPH);
+#pragma unroll
+        for (int c = 0; c < CPH; c += 8) {
+            uint4 p0, p1;
+            uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+            uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
+                const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
+                w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
+                w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
+            }
+            d0[c >> 3] = p0;
+            d1[c >> 3] = p1;
+        }
+    }
+}
+
 // Tile t -> (expert, first row, rows, n-block).  Tiles are ordered token-tile
 // major so the CTAs of one wave share an expert's token rows through L2 while
 // each streams distinct weight blocks.
@@ -96,23 +161,51 @@ __device__ __forceinline__ void decode_tile(int t, int nbc, int E, const int* mt
 // 128-row weight blocks -- consecutive ones, or gate block j and up block
 // N/256 + j with SiLU), 128-wide K blocks (48 KB stages, TMA, 128-byte
 // swizzle).  tcgen05.mma kind::f8f6f4 M=128 N=256 K=32 writes each K block's
-// partial into one of two 256-column TMEM buffers; 8 epilogue warps promote
-// it: thread (row r, column half h) owns 64 columns of each weight block and
-// needs just two scale products per K block (a_scale[r] * w_scale[block]),
-// then 128 FMAs.  SiLU pairs land in the same thread (gate column c and up
-// column 128 + c), so the fused epilogue needs no exchange.
+// partial into one of two 256-column TMEM buffers; the epilogue warps promote
+// it: thread (row r, column group h) owns 512 / (epilogue warps) columns of
+// each weight block and needs just two scale products per K block
+// (a_scale[r] * w_scale[block]), then one packed FMA per two columns.  SiLU
+// pairs land in the same thread (gate column c and up column 128 + c), so the
+// fused epilogue needs no exchange.
 // ---------------------------------------------------------------------------
-constexpr int kPfThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kPfEpi = 256;
+constexpr int kPfEpiWarps = 8;           // single-GPU form: epilogue warps (8 or 16)
+constexpr bool kPfRegSplit = false;      // single-GPU form: warpgroup 0 (TMA, MMA, 2 idle
+                                         // warps) hands registers to the epilogue warpgroups
+constexpr int kPfLdCols = 16;            // TMEM columns per tcgen05.ld in the epilogue (16 or 32)
+constexpr int kPfEpi0 = kPfRegSplit ? 4 : 2;                // first epilogue warp
+constexpr int kPfThreads = 32 * (kPfEpi0 + kPfEpiWarps);
 constexpr int kPfStage = 128 * 128 + 256 * 128;   // A 16 KB + B 32 KB
 constexpr int kPfMaxStages = 6;
 
 // The expert-parallel form adds six warps (warps 2-3 and a fourth warpgroup,
-// warps 12-15; the epilogue moves to warps 4-11): four pull the tile rows
-// from the peers and two push finished rows to them while the tile pipeline
-// runs.
+// warps 12-15; the epilogue is warps 4-11): four pull the tile rows from the
+// peers and two push finished rows to them while the tile pipeline runs.
 constexpr int kPfPullWarps = 4, kPfPushWarps = 2;
+constexpr int kPfEpEpiWarps = 8;
+constexpr int kPfEpLdCols = 16;         // its TMEM columns per tcgen05.ld (192-register epilogue)
 constexpr int kPfPeerThreads = 16 * 32;
+
+// Register split (setmaxnreg) of a launch with `threads` threads and one CTA
+// per SM.  Each of the 4 SM sub-partitions holds 16384 registers and every
+// 4th warp, so a thread gets 16384 / (32 x ceil(warps / 4)) rounded down to 8;
+// `ctl_warpgroups` warpgroups drop to `ctl` and the epilogue warps take what
+// is left (rounded down to 8, at most 256).  The sum never exceeds the
+// launch's registers, so every setmaxnreg.inc is satisfiable.
+__host__ __device__ constexpr int pf_launch_regs(int threads) {
+    return (16384 / (32 * ((threads / 32 + 3) / 4))) & ~7;
+}
+__host__ __device__ constexpr int pf_epi_regs(int threads, int ctl_warpgroups, int ctl,
+                                              int epi_warps) {
+    const int r =
+        ((pf_launch_regs(threads) * threads - 128 * ctl_warpgroups * ctl) / (32 * epi_warps)) & ~7;
+    return r > 256 ? 256 : r;
+}
+constexpr int kPfCtlRegs = 56;           // single-GPU form, warpgroup 0
+constexpr int kPfEpiRegs = pf_epi_regs(kPfThreads, 1, kPfCtlRegs, kPfEpiWarps);
+constexpr int kPfEpCtlRegs = 64;         // expert-parallel form, warpgroups 0 and 3
+constexpr int kPfEpEpiRegs = pf_epi_regs(kPfPeerThreads, 2, kPfEpCtlRegs, kPfEpEpiWarps);
+static_assert(!kPfRegSplit || kPfThreads % 128 == 0, "register split needs whole warpgroups");
+static_assert(kPfEpiWarps == 8 || kPfEpiWarps == 16, "8 or 16 epilogue warps");
 
 // waits for pulled rows to land / for a tile's rows to be stored before the push
 enum : int { SITE_ROWS = 11, SITE_PUSH = 12 };
@@ -185,6 +278,8 @@ __device__ __forceinline__ uint32_t ue8m0_word(float s) {
 
 constexpr int kPpStage = 128 * 128 + 128 * 128;    // A half 16 KB + B half 16 KB
 constexpr int kPpMaxStages = 6;
+constexpr int kPpEpiWarps = kPfEpiWarps;    // CTA-pair form: the single-CTA form's warp roles
+constexpr int kPpThreads = kPfThreads;
 
 enum : int { SITE_PEER_EMPTY = 9, SITE_PEER_TAIL = 10 };
 
@@ -204,7 +299,7 @@ __host__ __device__ inline PpLayout pp_layout(int stages, int E) {
     L.mts_off = o;
     o += 4 * (E + 1);
     L.part_off = o;
-    o += 4 * (kPfThreads + 1);
+    o += 4 * (kPpThreads + 1);
     o = (o + 7) & ~7;
     L.bar_off = o;
     o += 8 * (2 * kPpMaxStages + 2 * 2 + 1);

@@ -122,7 +122,7 @@ __device__ __forceinline__ void ep_push_rows(const EpMoveArgs& mv, const __nv_bf
                                              volatile int* abort_flag, const DevCtl& ctl) {
     const int vec = ldo >> 3;                  // 16-byte words per output row
     const int slots = mt_start[E] * 128;
-    const int want = nbc * (kPfEpi / 32);
+    const int want = nbc * kPfEpEpiWarps;
     for (int idx = blockIdx.x * kPfPushWarps + pw; idx < slots; idx += gridDim.x * kPfPushWarps) {
         const int mt = idx >> 7, i = idx & 127;
         int e, row0, rows, nb;
@@ -152,13 +152,16 @@ __device__ __forceinline__ void ep_push_rows(const EpMoveArgs& mv, const __nv_bf
 }
 
 // The tile pipeline of the prefill kernel and of its expert-parallel form.
-// REM: only the rows of each expert past its whole 256-row chunks (which the
-// CTA-pair kernel below takes), i.e. its last count % 256 rows.
 // EP: the expert-parallel form (EpMoveArgs), kPfPeerThreads threads.
-template <bool PAIR, bool REM, bool EP>
+template <bool PAIR, bool EP>
 __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUtensorMap* tm_a,
                                              const GemmArgs& args, const EpMoveArgs& mv) {
     constexpr int kNT = EP ? kPfPeerThreads : kPfThreads;
+    constexpr int kEW = EP ? kPfEpEpiWarps : kPfEpiWarps;      // epilogue warps
+    constexpr int kEpi0 = EP ? 4 : kPfEpi0;                    // first epilogue warp
+    constexpr int kCPH = 512 / kEW;          // columns per thread in each 128-column half
+    constexpr int kLDmax = EP ? kPfEpLdCols : kPfLdCols;
+    constexpr int kLD = kCPH < kLDmax ? kCPH : kLDmax;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -176,7 +179,6 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPfMaxStages + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * kPfMaxStages + 4);
-    const uint32_t epi_bar = drain_bar + 8u;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
     const uint32_t stage_base = smem_addr(smem + L.stages_off);
@@ -188,10 +190,9 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), kPfEpi);
+            mbar_init(tempty_bar(a), kEW);      // one arrive per epilogue warp
         }
         mbar_init(drain_bar, 1);
-        mbar_init(epi_bar, kPfEpi);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -214,10 +215,6 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
             s = min(max(s, 0), M);
             c = min(max(c, 0), M - s);
         }
-        if (REM) {
-            s += c & ~255;
-            c &= 255;
-        }
         seg_s[e] = s;
         seg_c[e] = c;
         mt_start[e] = (c + 127) >> 7;
@@ -230,7 +227,6 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int total = mt_start[E] * nbc;
-    constexpr int kEpi0 = EP ? 4 : 2;      // first epilogue warp
 
     auto producer = [&]() {
         // ================= TMA producer =================
@@ -303,7 +299,7 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
     };
     auto epilogue = [&]() {
         // ================= epilogue: promotion + store =================
-        const int h = (warp - kEpi0) >> 2;       // column half: [64h, 64h+64) of each block
+        const int h = (warp - kEpi0) >> 2;       // columns [kCPH h, kCPH (h+1)) of each block
         const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = tile rows
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
@@ -324,9 +320,9 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
             const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
             const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
             const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
-            float acc0[64], acc1[64];
+            float acc0[kCPH], acc1[kCPH];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
+            for (int j = 0; j < kCPH; ++j) {
                 acc0[j] = 0.0f;
                 acc1[j] = 0.0f;
             }
@@ -340,21 +336,13 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
                                                        args.ctl, SITE_TFULL));
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
-#pragma unroll
-                for (int c = 0; c < 64; c += 16) {
-                    float v[16], u[16];
-                    tmem_ld16(tb + c, v);
-                    tmem_ld16(tb + 128 + c, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
-                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
-                    }
-                }
+                promote_kblock<kCPH, kLD>(tmem_base + lane_addr + ra.slot * 256 + h * kCPH, acc0,
+                                          acc1, s0, s1);
+                // every lane's loads of this buffer are complete (wait::ld)
+                // before the warp's single arrive releases it to the MMA
                 tc_fence_before();
-                mbar_arrive(tempty_bar(ra.slot));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(ra.slot));
             }
             if (!ok) break;
             int orow = row0 + r;
@@ -362,43 +350,8 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
                 orow = __ldg(args.out_rows + row0 + r);
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
-            if (live && orow >= 0) {
-                __nv_bfloat16* o = out_row_ptr(args, orow, ldo);
-                if (PAIR) {
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
-#pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 pk;
-                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b = __floats2bfloat162_rn(
-                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
-                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
-                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
-                        }
-                        dst[c >> 3] = pk;
-                    }
-                } else {
-                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
-                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
-#pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 p0, p1;
-                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
-                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
-                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
-                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
-                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
-                        }
-                        d0[c >> 3] = p0;
-                        d1[c >> 3] = p1;
-                    }
-                }
-            }
+            if (live && orow >= 0)
+                store_tile_row<PAIR, kCPH>(out_row_ptr(args, orow, ldo), nb, h, acc0, acc1);
             if constexpr (EP) {
                 // this warp's rows of the tile are stored: count it for the push
                 __threadfence();
@@ -412,10 +365,11 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
         // Warpgroups 0 (TMA, MMA, pull, push) and 3 (pull x3, push) hand
         // registers to the two epilogue warpgroups (1, 2), which then hold their
         // accumulators without spilling: launched at 128 per thread, 2 x 128 x 64
-        // + 2 x 128 x 192 = 512 x 128, and per SM sub-partition
-        // 32 x (64 + 64 + 192 + 192) = 16384.
+        // + 2 x 128 x 192 = 512 x 128.
+        static_assert(kPfEpEpiWarps == 8 && kPfEpCtlRegs == 64 && kPfEpEpiRegs == 192,
+                      "warp roles below assume this split");
         if (warp < 4 || warp >= 12) {
-            setmaxnreg_dec<64>();
+            setmaxnreg_dec<kPfEpCtlRegs>();
             if (warp == 0) producer();
             else if (warp == 1) mma_issuer();
             else if (warp == 2 || warp >= 13)
@@ -424,7 +378,22 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
                 ep_push_rows(mv, args.out, PAIR ? (N >> 1) : N, nbc, E, mt_start, seg_s, seg_c,
                              warp == 3 ? 0 : 1, lane, abort_flag, args.ctl);
         } else {
-            setmaxnreg_inc<192>();
+            setmaxnreg_inc<kPfEpEpiRegs>();
+            epilogue();
+        }
+    } else if constexpr (kPfRegSplit) {
+        // warpgroup 0 (TMA, MMA; warps 2-3 idle) hands registers to the
+        // epilogue warpgroups (the launcher checks that the kernel was built
+        // with pf_launch_regs(kPfThreads) registers per thread)
+        static_assert(128 * kPfCtlRegs + 32 * kPfEpiWarps * kPfEpiRegs <=
+                          kPfThreads * pf_launch_regs(kPfThreads),
+                      "register split above the launch's registers");
+        if (warp < 4) {
+            setmaxnreg_dec<kPfCtlRegs>();
+            if (warp == 0) producer();
+            else if (warp == 1) mma_issuer();
+        } else {
+            setmaxnreg_inc<kPfEpiRegs>();
             epilogue();
         }
     } else {
@@ -443,12 +412,12 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
 }
 
 
-template <bool PAIR, bool REM = false>
+template <bool PAIR>
 __global__ void __launch_bounds__(kPfThreads, 1)
     fp8_w13_prefill_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
     pdl_begin();
-    prefill_body<PAIR, REM, false>(&tm_w, &tm_a, args, EpMoveArgs{});
+    prefill_body<PAIR, false>(&tm_w, &tm_a, args, EpMoveArgs{});
 }
 
 template <bool PAIR>
@@ -457,49 +426,47 @@ __global__ void __launch_bounds__(kPfPeerThreads, 1)
                               const __grid_constant__ CUtensorMap tm_a, const GemmArgs args,
                               const EpMoveArgs mv) {
     pdl_begin();
-    prefill_body<PAIR, false, true>(&tm_w, &tm_a, args, mv);
+    prefill_body<PAIR, true>(&tm_w, &tm_a, args, mv);
 }
 
 // ---------------------------------------------------------------------------
-// CTA-pair form of the prefill kernel (FERRET_PREFILL_PAIRS) for each expert's
-// whole 256-row chunks; the rows past them go to fp8_w13_prefill_kernel<.., true>.
+// CTA-pair form of the prefill kernel (FERRET_PREFILL_PAIRS).
 //
-// A pair (thread-block cluster of 2) computes a 256-token x 256-weight-row
-// tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32): CTA r holds
-// token rows [128r, 128r+128) of the tile and weight rows [128r, 128r+128)
-// (gate block for r = 0 and up block for r = 1 with SiLU), and receives the
-// 128 x 256 partial of its own token rows in its own Tensor Memory.  Per SM
-// that is 32 KB of operands per K block instead of 48 KB for the same MMA
-// work, so the L2->SM stream shrinks by a third and 6 stages fit.
+// A pair (thread-block cluster of 2 on two SMs) computes a 256-token x
+// 256-weight-row tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32):
+// CTA r loads token rows [128r, 128r+128) of the tile and weight rows
+// [128r, 128r+128) of its 256-row block (gate block for r = 0 and up block for
+// r = 1 with SiLU), and receives the 128 x 256 partial of its own token rows in
+// its own Tensor Memory.  Per SM that is 32 KB of operands per 128-wide K block
+// instead of 48 KB for the same MMA work, so the same shared-memory ring keeps
+// 1.5x more MMA work in flight.  Every expert's rows are covered by 256-row
+// pair tiles; in the last one the rows past the expert are computed and
+// dropped (a half with none of the expert's rows loads no A tile and skips its
+// promotion).
 //
 // Protocol (every load is a plain TMA load into the issuing CTA's own shared memory):
 //   * both CTAs load their halves with .cta_group::2 TMA, completing on the
-//     leader's (rank 0) full barrier, which the leader arms with both halves'
-//     bytes;
-//   * the leader's single MMA thread waits for it, issues the pair MMAs and
-//     commits to each CTA's empty barrier (stage free) and tfull barrier
-//     (K-block partial ready);
-//   * each CTA's 8 epilogue warps promote their own partial exactly as the
-//     single-CTA kernel does and release the buffer with one arrive per warp
-//     on the leader's tempty barrier (16 arrivals);
+//     leader's (rank 0) full barrier, which the leader arms with the tile's
+//     byte count of both CTAs;
+//   * the leader's MMA thread waits for it and for the TMEM buffer's release,
+//     issues the 4 pair MMAs of the K block and commits to each CTA's empty
+//     barrier (stage free) and tfull barrier (partial ready);
+//   * each CTA's epilogue warps promote their own partial exactly as the
+//     single-CTA kernel does and release the buffer with one arrive per warp on
+//     the leader's tempty barrier;
 //   * a cluster barrier after the roles finish keeps either CTA from leaving
-//     while the other still reads its shared memory or Tensor Memory.
-//
-// Measured on B200 (benchmark configuration 3, GEMM alone): 4.311 ms for this
-// kernel plus the single-CTA remainder launch, against 2.708 ms for the
-// single-CTA kernel alone.  With exact fp32 scales every K block's partial has
-// to be promoted by both CTAs before the leader can reuse one of the two TMEM
-// buffers, which puts a cross-SM round trip (tfull to the peer, the peer's
-// promotion, its arrive back on the leader) on every K block.  Hence opt-in;
-// the pair protocol itself is the base for the block-scaled pair tile, whose
-// single accumulator needs one such handshake per tile.
+//     while the other still reads its shared memory or writes its Tensor Memory.
 // ---------------------------------------------------------------------------
 
 template <bool PAIR>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __launch_bounds__(kPpThreads, 1)
     fp8_w13_prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_w,
                                 const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
     pdl_begin();
+    constexpr int kEW = kPpEpiWarps;
+    constexpr int kEpi0 = kPfEpi0;
+    constexpr int kCPH = 512 / kEW;
+    constexpr int kLD = kCPH < kPfLdCols ? kCPH : kPfLdCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -531,7 +498,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 2 * (kPfEpi / 32));   // one per epilogue warp of both CTAs
+            mbar_init(tempty_bar(a), 2 * kEW);   // one per epilogue warp of both CTAs
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -542,7 +509,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tmem_relinquish_pair();
     }
     bool seg_bad = false;
-    for (int e = tid; e < E; e += kPfThreads) {
+    for (int e = tid; e < E; e += kPpThreads) {
         int s, c;
         if (args.seg_pairs) {
             s = args.seg[2 * e];
@@ -557,8 +524,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             c = min(max(c, 0), M - s);
         }
         seg_s[e] = s;
-        seg_c[e] = c & ~255;                      // whole 256-row chunks only
-        mt_start[e] = c >> 8;
+        seg_c[e] = c;
+        mt_start[e] = (c + 255) >> 8;
     }
     if (seg_bad && leader) report(args.ctl, DEV_LAYOUT);
     __syncthreads();
@@ -570,7 +537,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
     const int total = mt_start[E] * nbc;
 
-    if (warp == 0) {
+    auto producer = [&]() {
         // ================= TMA producer (both CTAs) =================
         if (elect_one()) {
             tma_prefetch_desc(&tm_w);
@@ -582,6 +549,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int t = pair; t < total && ok; t += npairs) {
                 int e, row0, rows, nb;
                 decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
+                const bool a_live = 128 * (int)rank < rows;      // this CTA's A rows exist
+                const uint32_t bytes = 3 * 16384 + (rows > 128 ? 16384 : 0);
                 const int arow = row0 + 128 * (int)rank;
                 const int wrow = PAIR ? e * N + (rank ? (N >> 1) : 0) + nb * 128
                                       : e * N + nb * 256 + 128 * (int)rank;
@@ -592,10 +561,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_expect_tx(full_bar(s), 2 * kPpStage);
+                    if (leader) mbar_expect_tx(full_bar(s), bytes);
                     const uint32_t dst = stage_base + s * kPpStage;
                     const uint32_t bar = mapa_shared(full_bar(s), 0);
-                    tma_load_2d_pair(dst, &tm_a, kb * 128, arow, bar, pol);
+                    if (a_live) tma_load_2d_pair(dst, &tm_a, kb * 128, arow, bar, pol);
                     tma_load_2d_pair(dst + 16384, &tm_w, kb * 128, wrow, bar, pol);
                 }
             }
@@ -606,7 +575,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                   SITE_PEER_TAIL, false))
                     break;
         }
-    } else if (warp == 1) {
+    };
+    auto mma_issuer = [&]() {
         // ================= MMA issuer (leader CTA) =================
         if (leader && elect_one()) {
             constexpr uint32_t idesc = make_idesc(256, 256, 0, 0);
@@ -637,9 +607,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_commit_pair(drain_bar);
             mbar_wait(drain_bar, 0, abort_flag, args.ctl, SITE_DRAIN, false);
         }
-    } else {
+    };
+    auto epilogue = [&]() {
         // ================= epilogue: promotion + store (both CTAs) =================
-        const int h = (warp - 2) >> 2;           // column half: [64h, 64h+64) of each block
+        const int h = (warp - kEpi0) >> 2;       // columns [kCPH h, kCPH (h+1)) of each block
         const int q = warp & 3;                  // TMEM lanes [32q, 32q+32) = this CTA's rows
         const int r = q * 32 + lane;
         const int ldo = PAIR ? (N >> 1) : N;
@@ -649,15 +620,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             int e, row0, rows, nb;
             decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
             const int my0 = row0 + 128 * (int)rank;
-            const bool live = 128 * (int)rank + r < rows;
+            const int my_rows = min(max(rows - 128 * (int)rank, 0), 128);
+            const bool live = r < my_rows;
             const float* as_row = args.a_scale + (size_t)(my0 + (live ? r : 0)) * nk;
             const int blk0 = PAIR ? nb : 2 * nb;
             const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
             const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
             const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
-            float acc0[64], acc1[64];
+            float acc0[kCPH], acc1[kCPH];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
+            for (int j = 0; j < kCPH; ++j) {
                 acc0[j] = 0.0f;
                 acc1[j] = 0.0f;
             }
@@ -669,19 +641,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                                           args.ctl, SITE_TFULL));
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t tb = tmem_base + lane_addr + ra.slot * 256 + h * 64;
-#pragma unroll
-                for (int c = 0; c < 64; c += 16) {
-                    float v[16], u[16];
-                    tmem_ld16(tb + c, v);
-                    tmem_ld16(tb + 128 + c, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
-                        acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
-                    }
-                }
+                if (my_rows > 0)
+                    promote_kblock<kCPH, kLD>(tmem_base + lane_addr + ra.slot * 256 + h * kCPH,
+                                              acc0, acc1, s0, s1);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(ra.slot), 0));
@@ -692,49 +654,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 orow = __ldg(args.out_rows + my0 + r);
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
-            if (live && orow >= 0) {
-                __nv_bfloat16* o = args.out + (size_t)orow * ldo;
-                if (PAIR) {
-                    uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * 64);
-#pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 pk;
-                        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b = __floats2bfloat162_rn(
-                                silu_mul(acc0[c + 2 * j], acc1[c + 2 * j]),
-                                silu_mul(acc0[c + 2 * j + 1], acc1[c + 2 * j + 1]));
-                            pw[j] = *reinterpret_cast<const uint32_t*>(&b);
-                        }
-                        dst[c >> 3] = pk;
-                    }
-                } else {
-                    uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * 64);
-                    uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * 64);
-#pragma unroll
-                    for (int c = 0; c < 64; c += 8) {
-                        uint4 p0, p1;
-                        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
-                        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0[c + 2 * j], acc0[c + 2 * j + 1]);
-                            const __nv_bfloat162 b1 = __floats2bfloat162_rn(acc1[c + 2 * j], acc1[c + 2 * j + 1]);
-                            w0[j] = *reinterpret_cast<const uint32_t*>(&b0);
-                            w1[j] = *reinterpret_cast<const uint32_t*>(&b1);
-                        }
-                        d0[c >> 3] = p0;
-                        d1[c >> 3] = p1;
-                    }
-                }
-            }
+            if (live && orow >= 0)
+                store_tile_row<PAIR, kCPH>(args.out + (size_t)orow * ldo, nb, h, acc0, acc1);
         }
+    };
+
+    if constexpr (kPfRegSplit) {
+        if (warp < 4) {
+            setmaxnreg_dec<kPfCtlRegs>();
+            if (warp == 0) producer();
+            else if (warp == 1) mma_issuer();
+        } else {
+            setmaxnreg_inc<kPfEpiRegs>();
+            epilogue();
+        }
+    } else {
+        if (warp == 0) producer();
+        else if (warp == 1) mma_issuer();
+        else epilogue();
     }
 
     tc_fence_before();
     __syncthreads();
-    cluster_sync();                               // the pair's MMAs and arrivals are done
+    cluster_sync();             // neither CTA leaves while the other may still touch it
     tc_fence_after();
     if (warp == 1) {
         __syncwarp();
@@ -744,9 +686,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
 template <bool PAIR>
 int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const float* a_scale,
-                             const void* w, const float* w_scale, void* out, const int32_t* seg,
-                             int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
-                             const OutMap& om) {
+                               const void* w, const float* w_scale, void* out, const int32_t* seg,
+                               int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
+                               const OutMap& om) {
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
                           128, true);
@@ -762,7 +704,9 @@ int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const floa
         cudaGetLastError();
         return FERRET_ERR_CUDA;
     }
-    const int pairs = std::min(max_resident_pairs(kern, dim3(kPfThreads), smem), info->num_sms / 2);
+    static const bool regs_ok = !kPfRegSplit || kernel_has_regs(kern, pf_launch_regs(kPpThreads));
+    if (!regs_ok) return FERRET_ERR_CUDA;
+    const int pairs = std::min(max_resident_pairs(kern, dim3(kPpThreads), smem), info->num_sms / 2);
     if (pairs < 1) return FERRET_ERR_UNSUPPORTED;
     GemmArgs g;
     g.a_scale = a_scale;
@@ -780,22 +724,9 @@ int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const floa
     g.E = E;
     g.stages = stages;
     g.ctl = make_ctl(info);
-    rc = launch_kernel_pairs(kern, dim3(2 * pairs), dim3(kPfThreads), smem, stream, tm_w, tm_a, g);
-    if (rc != FERRET_OK) return rc;
-    // the rows past each expert's whole 256-row chunks
-    const int stages1 = std::min(kPfMaxStages, (budget - pf_layout(0, E, false).total) / kPfStage);
-    if (stages1 < 2) return FERRET_ERR_SHAPE;
-    const int smem1 = pf_layout(stages1, E, false).total + 1024;
-    auto kern1 = fp8_w13_prefill_kernel<PAIR, true>;
-    if (cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) !=
-        cudaSuccess) {
-        cudaGetLastError();
-        return FERRET_ERR_CUDA;
-    }
-    g.stages = stages1;
-    return launch_kernel(kern1, dim3(info->num_sms), dim3(kPfThreads), smem1, stream, tm_w, tm_a, g);
+    return launch_kernel_pairs(kern, dim3(2 * pairs), dim3(kPpThreads), smem, stream, tm_w, tm_a,
+                               g);
 }
-
 
 template <bool PAIR, bool EP>
 int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_scale, const void* w,
@@ -836,8 +767,14 @@ int launch_fp8_prefill_t(const DeviceInfo* info, const void* a, const float* a_s
     g.E = E;
     g.stages = stages;
     g.ctl = make_ctl(info);
-    if (!EP) return launch_kernel(kern_local, dim3(info->num_sms), dim3(kPfThreads), smem, stream,
-                                  tm_w, tm_a, g);
+    if (!EP) {
+        static const bool regs_ok = !kPfRegSplit || kernel_has_regs(kern_local, pf_launch_regs(kPfThreads));
+        if (!regs_ok) return FERRET_ERR_CUDA;
+        return launch_kernel(kern_local, dim3(info->num_sms), dim3(kPfThreads), smem, stream, tm_w,
+                             tm_a, g);
+    }
+    static const bool regs_ok_ep = kernel_has_regs(kern_ep, pf_launch_regs(kPfPeerThreads));
+    if (!regs_ok_ep) return FERRET_ERR_CUDA;
     if (!om.rows || !om.peers || !om.q_peers || !om.s_peers || !om.ready || !om.done ||
         om.peer_rows <= 0 || om.gather_topk <= 0)
         return FERRET_ERR_NULL;

@@ -291,16 +291,17 @@ PAIR_CASES = [
     ([600, 0, 256, 255, 1000, 3], 512, 512, True),
     ([1024], 256, 7168, False),
     ([513, 770], 1024, 384, True),
-    ([100, 37], 256, 256, False),                   # no whole chunk: the single-CTA part only
+    ([100, 37], 256, 256, False),                   # one pair tile per expert, second half empty
 ]
 
 
 @pytest.mark.parametrize("seg,N,K,silu", PAIR_CASES)
 @pytest.mark.parametrize("use_offsets", [False, True])
 def test_grouped_gemm_cta_pairs_vs_oracle(ops, seg, N, K, silu, use_offsets):
-    """FERRET_PREFILL_PAIRS: tcgen05.mma.cta_group::2 tiles for each expert's
-    whole 256-row chunks against the oracle, and equal to the single-CTA
-    prefill kernel (same per-K-block promotion order)."""
+    """FERRET_PREFILL_PAIRS: tcgen05.mma.cta_group::2 tiles of 256 rows over
+    every expert's rows (the last one of an expert partly or half empty)
+    against the oracle, and equal to the single-CTA prefill kernel (same
+    per-K-block promotion order)."""
     a, a_s, w, w_s, mi = make_case(hash((tuple(seg), N, K, 2)) & 0xFFFF, seg, N, K)
     M = len(mi)
     outs = []
