@@ -279,19 +279,23 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
     return r;
 }
 
-// Arrive on an mbarrier of either CTA of the cluster (release, cluster scope).
+// Arrive on an mbarrier of either CTA of the cluster, with the default
+// semantics (release at CTA scope) of a local arrive.  The handoffs it signals
+// are ordered by the tcgen05 fences around it (Tensor Memory reads finished
+// before a buffer is released); a cluster-scope release would also make every
+// call wait for a memory fence, once per warp and K block.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
 }
 
-// try_wait with acquire at cluster scope (the barrier receives arrivals from
-// the peer CTA), with the suspend-time hint.
+// try_wait with the suspend-time hint for a barrier that also receives
+// arrivals from the peer CTA (tcgen05.commit, TMA byte counts, remote
+// arrives); default acquire semantics, as for the local waits.
 __device__ __forceinline__ bool mbar_test_cl(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred P;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, P;\n\t}"
         : "=r"(done)
         : "r"(bar), "r"(parity), "r"(hint_ns)
