@@ -37,6 +37,18 @@
 // each item's K blocks are split over several units; fp32 partials go to the
 // workspace and the last unit of an item (atomic counter) sums them in split
 // order -- deterministic -- and stores.
+//
+// Feeding the warps.  A warp that loads its own weights from global memory
+// can keep only one K block of loads in flight (its registers hold them), far
+// fewer bytes per SM than it takes to cover the HBM latency.  So a fifth warp
+// copies each K block into a shared-memory ring ahead of use: the weight blob
+// of the (expert, 128-row block, K block) -- 9 KB contiguous, one bulk copy;
+// two with SiLU -- and the pass's 8 activation rows of that K block (one 2 KB
+// tensor-map box; rows past the expert are computed and never stored).  The
+// four math warps read their fragments from shared memory and release the
+// stage before the MMAs.  The blob's 16-byte chunks are XOR-swizzled by the
+// repack (chunk c of word row k8 stored at c ^ 2 (k8 % 4)), which makes the
+// fragment reads -- 8 lanes at 4 word rows x 2 chunks -- conflict-free.
 #include <algorithm>
 
 #include "int4_common.cuh"
@@ -44,22 +56,28 @@
 namespace ferret {
 namespace {
 
-constexpr int kRdWarps = 4;                 // 4 warps x 32 weight rows = one 128-row block
-constexpr int kRdThreads = kRdWarps * 32;
+constexpr int kRdWarps = 4;                 // math warps: 4 x 32 weight rows = one 128-row block
+constexpr int kRdMath = kRdWarps * 32;
+constexpr int kRdThreads = kRdMath + 32;    // + the copy warp
 constexpr int kRdTok = 8;                   // token rows per pass: the MMA's N
 constexpr int kRdMaxE = 1024;
-constexpr int kRdBlobWords = 2304;          // 2048 packed words [k8][n] + 256 scale words
+constexpr int kRdBlob = 9216;               // bytes: 2048 packed words [k8][n] + 512 scale words
+constexpr int kRdXTile = kRdTok * 128 * 2;  // 8 token rows x 128 K values, bf16
 constexpr int kRdPart = 16;                 // fp32 partials per thread (4 accumulators x 4)
+constexpr int kRdCtas = 3;                  // CTAs per SM
+constexpr int kRdMaxStages = 8;
+
+enum : int { RD_EMPTY = 1, RD_FULL = 2, RD_DRAIN = 3 };
 
 struct Int4DecArgs {
-    const uint32_t* blob;                   // repacked blobs [E][N/128][K/128] x 2304 words
-    const __nv_bfloat16* a;                 // [R, K] expert-sorted activation rows
+    const uint8_t* blob;                    // repacked blobs [E][N/128][K/128] x kRdBlob
     const int32_t* sorted_rows;             // (token, slot) index of each sorted row
     const int32_t* offsets;                 // [E+1]
     __nv_bfloat16* out;                     // [T*topk, N or N/2] in (token, slot) order
     int N, K, E, R;
     int splits;                             // K splits per item (1: none)
-    float* part;                            // [unit][kRdThreads][kRdPart]
+    int stages;
+    float* part;                            // [unit][kRdMath][kRdPart]
     int* cnt;                               // [item] finished units, zero at launch
     DevCtl ctl;
 };
@@ -91,82 +109,155 @@ __device__ __forceinline__ void group_mma(const uint4 w, const uint2 sc, const u
     mma_16816(acc1, d2.z, d3.z, d2.w, d3.w, x.z, x.w);
 }
 
+// Unit u -> (expert, first sorted row of the pass, live rows, output block,
+// K-block range); the copy warp and the math warps walk the same sequence.
+struct RdUnit {
+    int item, e, r0, cc, ob, kb0, kb1;
+};
+
+__device__ __forceinline__ RdUnit rd_unit(int u, int S, int E, int nob, int nk,
+                                          const int* it_start, const int32_t* offsets) {
+    RdUnit w;
+    w.item = u / S;
+    const int s = u - w.item * S;
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (it_start[mid] <= w.item) lo = mid;
+        else hi = mid - 1;
+    }
+    w.e = lo;
+    const int local = w.item - it_start[w.e];
+    const int pass = local / nob;
+    w.ob = local - pass * nob;
+    w.r0 = __ldg(offsets + w.e) + pass * kRdTok;
+    w.cc = min(kRdTok, __ldg(offsets + w.e + 1) - w.r0);
+    w.kb0 = s * nk / S;
+    w.kb1 = (s + 1) * nk / S;
+    return w;
+}
+
 template <bool PAIR>
-__global__ void __launch_bounds__(kRdThreads, 4)
-    int4_w13_decode_kernel(const Int4DecArgs args) {
+__global__ void __launch_bounds__(kRdThreads, kRdCtas)
+    int4_w13_decode_kernel(const __grid_constant__ CUtensorMap tm_x, const Int4DecArgs args) {
     pdl_begin();
+    constexpr int kW = PAIR ? 2 : 1;
+    constexpr int kStage = kW * kRdBlob + kRdXTile;    // multiple of 1024
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     __shared__ int it_start[kRdMaxE + 1];
     __shared__ int scan_part[kRdThreads + 1];
+    __shared__ __align__(8) uint64_t bars[2 * kRdMaxStages];
     __shared__ int s_last;
+    __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int N = args.N, K = args.K, E = args.E;
+    const int N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7, nbn = N >> 7;
     const int nob = PAIR ? N >> 8 : N >> 7;          // 128-column output blocks
     const int ldo = PAIR ? N >> 1 : N;
     const int S = args.splits;
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kRdMaxStages + s); };
+    volatile int* abort_flag = &s_abort;
 
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), kRdWarps);
+        }
+        s_abort = 0;
+        mbar_init_fence();
+    }
     for (int e = tid; e < E; e += kRdThreads) {
         const int c = __ldg(args.offsets + e + 1) - __ldg(args.offsets + e);
         it_start[e] = c > 0 ? ((c + kRdTok - 1) / kRdTok) * nob : 0;
     }
     __syncthreads();
-    block_exclusive_scan(it_start, E, scan_part);
-    const int items = it_start[E];
+    block_exclusive_scan(it_start, E, scan_part);   // ends with __syncthreads
+    const int units = it_start[E] * S;
 
-    for (int u = blockIdx.x; u < items * S; u += gridDim.x) {
-        const int item = u / S, s = u - item * S;
-        int lo = 0, hi = E - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (it_start[mid] <= item) lo = mid;
-            else hi = mid - 1;
+    if (warp == kRdWarps) {
+        // ================= copy warp =================
+        if (elect_one()) {
+            tma_prefetch_desc(&tm_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            RingPos rp;
+            int it = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const RdUnit w = rd_unit(u, S, E, nob, nk, it_start, args.offsets);
+                const uint8_t* bg = args.blob + ((size_t)w.e * nbn + w.ob) * nk * kRdBlob;
+                const uint8_t* bu = args.blob + ((size_t)w.e * nbn + w.ob + (N >> 8)) * nk * kRdBlob;
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++it, rp.advance(NS)) {
+                    if (!mbar_wait(empty_bar(rp.slot), rp.phase ^ 1u, abort_flag, args.ctl, RD_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = smem_addr(ring + rp.slot * kStage);
+                    mbar_expect_tx(full_bar(rp.slot), kStage);
+                    bulk_load_hint(st, bg + (size_t)kb * kRdBlob, kRdBlob, full_bar(rp.slot), pol_w);
+                    if (PAIR)
+                        bulk_load_hint(st + kRdBlob, bu + (size_t)kb * kRdBlob, kRdBlob,
+                                       full_bar(rp.slot), pol_w);
+                    tma_load_2d_hint(st + kW * kRdBlob, &tm_x, kb * 128, w.r0, full_bar(rp.slot),
+                                     pol_x);
+                }
+            }
+            // the copies into the last stages land before the CTA may exit
+            for (int i = max(0, it - NS); i < it; ++i)
+                mbar_wait(full_bar(i % NS), (i / NS) & 1, abort_flag, args.ctl, RD_DRAIN, false);
         }
-        const int e = lo;
-        const int local = item - it_start[e];
-        const int pass = local / nob, ob = local - pass * nob;
-        const int r0 = __ldg(args.offsets + e) + pass * kRdTok;
-        const int cc = min(kRdTok, __ldg(args.offsets + e + 1) - r0);
-        const int kb0 = s * nk / S, kb1 = (s + 1) * nk / S;
+        return;
+    }
 
-        // this thread's rows: 32*warp + 4g .. +3 of the gate (or plain) block
-        // and of the up block
-        const int nb_g = ob, nb_u = ob + (N >> 8);
-        const uint32_t* bg = args.blob + ((size_t)e * nbn + nb_g) * nk * kRdBlobWords;
-        const uint32_t* bu = args.blob + ((size_t)e * nbn + nb_u) * nk * kRdBlobWords;
-        const int wrow = 32 * warp + 4 * g;
-        const bool live = g < cc;
-        const __nv_bfloat16* xrow = args.a + (size_t)(r0 + (live ? g : 0)) * K;
-
+    // ================= math warps =================
+    const int g = lane >> 2, t = lane & 3;
+    const int wrow = 32 * warp + 4 * g;             // this thread's rows: wrow .. wrow + 3
+    // fragment offsets inside a stage (bytes): word row k8 = 4q + t of the
+    // swizzled blob, the scale pair words of group q, token row g's 8 values
+    const int w_off = (t * 128 + (wrow ^ (t << 3))) * 4;
+    const int s_off = 8192 + ((wrow >> 1) * 4);
+    const int x_off = kW * kRdBlob + g * 256 + t * 16;
+    RingPos rs;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const RdUnit w = rd_unit(u, S, E, nob, nk, it_start, args.offsets);
         float ag0[4] = {0, 0, 0, 0}, ag1[4] = {0, 0, 0, 0};
         float au0[4] = {0, 0, 0, 0}, au1[4] = {0, 0, 0, 0};
-        for (int kb = kb0; kb < kb1; ++kb) {
-            const uint32_t* wg = bg + (size_t)kb * kRdBlobWords;
-            const uint32_t* wu = bu + (size_t)kb * kRdBlobWords;
+        bool ok = true;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, rs.advance(NS)) {
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(full_bar(rs.slot), rs.phase, abort_flag, args.ctl, RD_FULL));
+            if (!ok) break;
+            const uint8_t* st = ring + rs.slot * kStage;
             uint4 vg[4], vu[4], x[4];
             uint2 sg[4], su[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                vg[q] = __ldcs(reinterpret_cast<const uint4*>(wg + (4 * q + t) * 128 + wrow));
-                sg[q] = __ldcs(reinterpret_cast<const uint2*>(wg + 2048 + ((q * 128 + wrow) >> 1)));
+                vg[q] = *reinterpret_cast<const uint4*>(st + w_off + q * 4 * 512);
+                sg[q] = *reinterpret_cast<const uint2*>(st + s_off + q * 256);
                 if (PAIR) {
-                    vu[q] = __ldcs(reinterpret_cast<const uint4*>(wu + (4 * q + t) * 128 + wrow));
-                    su[q] = __ldcs(reinterpret_cast<const uint2*>(wu + 2048 + ((q * 128 + wrow) >> 1)));
+                    vu[q] = *reinterpret_cast<const uint4*>(st + kRdBlob + w_off + q * 4 * 512);
+                    su[q] = *reinterpret_cast<const uint2*>(st + kRdBlob + s_off + q * 256);
                 }
-                x[q] = live ? __ldg(reinterpret_cast<const uint4*>(xrow + kb * 128 + 8 * (4 * q + t)))
-                            : make_uint4(0, 0, 0, 0);
+                x[q] = *reinterpret_cast<const uint4*>(st + x_off + q * 64);
             }
+            // the fragments are in registers: the stage can be refilled
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(rs.slot));
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 group_mma(vg[q], sg[q], x[q], ag0, ag1);
                 if (PAIR) group_mma(vu[q], su[q], x[q], au0, au1);
             }
         }
+        if (!ok) break;
 
         // accumulator element i of slice h: weight row wrow + 2h + (i >> 1),
         // token 2t + (i & 1)
         if (S > 1) {
-            float* my = args.part + ((size_t)u * kRdThreads + tid) * kRdPart;
+            float* my = args.part + ((size_t)u * kRdMath + tid) * kRdPart;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 my[i] = ag0[i];
@@ -177,9 +268,9 @@ __global__ void __launch_bounds__(kRdThreads, 4)
                 }
             }
             __threadfence();
-            __syncthreads();
-            if (tid == 0) s_last = atomicAdd(args.cnt + item, 1) == S - 1;
-            __syncthreads();
+            named_bar_sync(1, kRdMath);
+            if (tid == 0) s_last = atomicAdd(args.cnt + w.item, 1) == S - 1;
+            named_bar_sync(1, kRdMath);
             if (!s_last) continue;
             __threadfence();
 #pragma unroll
@@ -187,7 +278,7 @@ __global__ void __launch_bounds__(kRdThreads, 4)
                 ag0[i] = ag1[i] = au0[i] = au1[i] = 0.0f;
             }
             for (int j = 0; j < S; ++j) {    // split order: deterministic
-                const float* p = args.part + ((size_t)(item * S + j) * kRdThreads + tid) * kRdPart;
+                const float* p = args.part + ((size_t)(w.item * S + j) * kRdMath + tid) * kRdPart;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     ag0[i] += __ldcg(p + i);
@@ -203,8 +294,8 @@ __global__ void __launch_bounds__(kRdThreads, 4)
 #pragma unroll
         for (int jt = 0; jt < 2; ++jt) {
             const int j = 2 * t + jt;
-            if (j >= cc) continue;
-            const int orow = __ldg(args.sorted_rows + r0 + j);
+            if (j >= w.cc) continue;
+            const int orow = __ldg(args.sorted_rows + w.r0 + j);
             float v[4] = {ag0[jt], ag0[2 + jt], ag1[jt], ag1[2 + jt]};
             if (PAIR) {
                 const float u4[4] = {au0[jt], au0[2 + jt], au1[jt], au1[2 + jt]};
@@ -216,9 +307,70 @@ __global__ void __launch_bounds__(kRdThreads, 4)
             uint2 pk;
             pk.x = *reinterpret_cast<const uint32_t*>(&p0);
             pk.y = *reinterpret_cast<const uint32_t*>(&p1);
-            *reinterpret_cast<uint2*>(args.out + (size_t)orow * ldo + ob * 128 + wrow) = pk;
+            *reinterpret_cast<uint2*>(args.out + (size_t)orow * ldo + w.ob * 128 + wrow) = pk;
         }
     }
+}
+
+template <bool PAIR>
+int launch_int4_decode_t(const DeviceInfo* info, const void* a_sorted, const uint8_t* blob,
+                         const int32_t* sorted_rows, const int32_t* offsets, void* out, int N,
+                         int K, int E, int R, cudaStream_t stream, uint8_t* split_ws,
+                         size_t split_bytes, int ncnt) {
+    if (E > kRdMaxE) return FERRET_ERR_SHAPE;
+    constexpr int kStage = (PAIR ? 2 : 1) * kRdBlob + kRdXTile;
+    CUtensorMap tm_x;
+    int rc = make_tmap_2d(&tm_x, a_sorted, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, (uint64_t)K * 2,
+                          128, kRdTok, false);
+    if (rc != FERRET_OK) return rc;
+    // stages: what kRdCtas CTAs per SM leave each (1 KB reserved per CTA, the
+    // static arrays, 1 KB of alignment slack)
+    const int per_cta = 233472 / kRdCtas - 1024 - (kRdMaxE + 1) * 4 - (kRdThreads + 1) * 4 - 256;
+    const int stages = std::min(kRdMaxStages, (per_cta - 1024) / kStage);
+    if (stages < 2) return FERRET_ERR_SHAPE;
+    const int smem = stages * kStage + 1024;
+    auto kern = int4_w13_decode_kernel<PAIR>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kRdThreads, smem) != cudaSuccess ||
+        occ < 1) {
+        cudaGetLastError();
+        return FERRET_ERR_CUDA;
+    }
+    Int4DecArgs a;
+    a.blob = blob;
+    a.sorted_rows = sorted_rows;
+    a.offsets = offsets;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.N = N;
+    a.K = K;
+    a.E = E;
+    a.R = R;
+    a.stages = stages;
+    a.ctl = make_ctl(info);
+    a.splits = 1;
+    a.part = nullptr;
+    a.cnt = nullptr;
+    const int grid = info->num_sms * std::min(occ, kRdCtas);
+    // Split K when the items cannot fill the resident CTAs: at most the bound
+    // on items, splits of at least 2 K blocks, if the workspace holds the
+    // partials (the counters, ncnt ints at split_ws, were cleared by the row
+    // gather).
+    const long long items_up = int4_decode_items_bound(R, E, N, PAIR);
+    if (split_ws && items_up > 0 && items_up <= ncnt) {
+        const int S = (int)std::min<long long>(grid / items_up, (K / 128) / 2);
+        const size_t cnt_bytes = ((size_t)items_up * sizeof(int) + 255) & ~size_t(255);
+        const size_t part_bytes = (size_t)items_up * S * kRdMath * kRdPart * sizeof(float);
+        if (S >= 2 && cnt_bytes + part_bytes <= split_bytes) {
+            a.splits = S;
+            a.cnt = reinterpret_cast<int*>(split_ws);
+            a.part = reinterpret_cast<float*>(split_ws + cnt_bytes);
+        }
+    }
+    return launch_kernel(kern, dim3(grid), dim3(kRdThreads), smem, stream, tm_x, a);
 }
 
 }  // namespace
@@ -229,40 +381,10 @@ int launch_int4_decode(const DeviceInfo* info, const void* a_sorted, const uint8
                        uint8_t* split_ws, size_t split_bytes, int ncnt) {
     (void)T;
     (void)topk;
-    if (E > kRdMaxE) return FERRET_ERR_SHAPE;
-    Int4DecArgs a;
-    a.blob = reinterpret_cast<const uint32_t*>(blob);
-    a.a = static_cast<const __nv_bfloat16*>(a_sorted);
-    a.sorted_rows = sorted_rows;
-    a.offsets = offsets;
-    a.out = static_cast<__nv_bfloat16*>(out);
-    a.N = N;
-    a.K = K;
-    a.E = E;
-    a.R = R;
-    a.ctl = make_ctl(info);
-    a.splits = 1;
-    a.part = nullptr;
-    a.cnt = nullptr;
-    constexpr int kCtasPerSm = 4;
-    const int grid = info->num_sms * kCtasPerSm;
-    // Split K when the items cannot fill the resident CTAs: at most the bound
-    // on items, splits of at least 2 K blocks, if the workspace holds the
-    // partials (the counters, ncnt ints at split_ws, were cleared by the row
-    // gather).
-    const long long items_up = int4_decode_items_bound(R, E, N, pair);
-    if (split_ws && items_up > 0 && items_up <= ncnt) {
-        const int S = (int)std::min<long long>(grid / items_up, (K / 128) / 2);
-        const size_t cnt_bytes = ((size_t)items_up * sizeof(int) + 255) & ~size_t(255);
-        const size_t part_bytes = (size_t)items_up * S * kRdThreads * kRdPart * sizeof(float);
-        if (S >= 2 && cnt_bytes + part_bytes <= split_bytes) {
-            a.splits = S;
-            a.cnt = reinterpret_cast<int*>(split_ws);
-            a.part = reinterpret_cast<float*>(split_ws + cnt_bytes);
-        }
-    }
-    return pair ? launch_kernel(int4_w13_decode_kernel<true>, dim3(grid), dim3(kRdThreads), 0, stream, a)
-                : launch_kernel(int4_w13_decode_kernel<false>, dim3(grid), dim3(kRdThreads), 0, stream, a);
+    return pair ? launch_int4_decode_t<true>(info, a_sorted, blob, sorted_rows, offsets, out, N, K,
+                                             E, R, stream, split_ws, split_bytes, ncnt)
+                : launch_int4_decode_t<false>(info, a_sorted, blob, sorted_rows, offsets, out, N, K,
+                                              E, R, stream, split_ws, split_bytes, ncnt);
 }
 
 }  // namespace ferret

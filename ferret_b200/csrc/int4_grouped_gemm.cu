@@ -14,7 +14,10 @@
 // activation row and separate scale boxes):
 //   * load time (ferret_int4_repack_w13): every 128 (n) x 128 (k) weight block
 //     and its 128 x 4 bf16 group scales become one contiguous 9 KB blob, nibbles
-//     reordered so each (k, k+1) pair sits 16 bits apart;
+//     reordered so each (k, k+1) pair sits 16 bits apart, and word row k8's
+//     entry for weight row n stored at n ^ 8 (k8 % 4) (which keeps this
+//     kernel's per-row reads conflict-free and makes the decode kernel's
+//     16-byte fragment reads so);
 //   * per call, a gather pass writes the expert-sorted activation rows
 //     contiguously (workspace), so one tensor-map box brings NT token rows of
 //     a 64-wide K half in the 128-byte-swizzled layout;
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
                         uint32_t wv[8];
                         uint32_t s0 = sc[(2 * h) * 128 + n], s1 = sc[(2 * h + 1) * 128 + n];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) wv[i] = words[(8 * h + i) * 128 + n];
+                        for (int i = 0; i < 8; ++i) wv[i] = words[(8 * h + i) * 128 + (n ^ ((i & 3) << 3))];
                         s0 |= s0 << 16;
                         s1 |= s1 << 16;
                         uint32_t r[32];
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(kI4Threads, 1)
 }
 
 // Load-time repack into 9 KB blobs: block (e, nb, kb) = 2048 words
-// [k8][n] with the nibbles of each word reordered to K offsets
+// [k8][n ^ 8 (k8 % 4)] with the nibbles of each word reordered to K offsets
 // {0,2,4,6,1,3,5,7}, then 4 x 128 bf16 scales [g][n].
 __global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint16_t* __restrict__ sc,
                                    uint32_t* __restrict__ blob, int E, int K, int N) {
@@ -480,7 +483,7 @@ __global__ void int4_repack_kernel(const uint32_t* __restrict__ raw, const uint1
         const int e = (int)(b / ((size_t)nbk * nbn));
         uint32_t r;
         if (w < 2048) {
-            const int k8 = w >> 7, n = w & 127;
+            const int k8 = w >> 7, n = (w & 127) ^ ((k8 & 3) << 3);
             const uint32_t v = raw[((size_t)e * (K >> 3) + kb * 16 + k8) * N + nb * 128 + n];
             r = 0;
 #pragma unroll

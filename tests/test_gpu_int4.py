@@ -48,7 +48,8 @@ def run(ops, h, rq, sc, ids, silu, tile=0):
 
 
 def test_repack_blob_layout(ops):
-    """Blob (e, nb, kb) = 2048 nibble-permuted words [k8][n] + bf16 scales [g][n]."""
+    """Blob (e, nb, kb) = 2048 nibble-permuted words [k8][n ^ 8 (k8 % 4)] + bf16
+    scales [g][n]."""
     rng = np.random.default_rng(0)
     E, K, N = 2, 256, 256
     raw = rng.integers(-2**31, 2**31 - 1, size=(E, K // 8, N), dtype=np.int64).astype(np.int32)
@@ -68,7 +69,8 @@ def test_repack_blob_layout(ops):
                 want = np.zeros_like(src)
                 for slot, k in enumerate(perm):
                     want |= ((src >> np.uint32(4 * k)) & np.uint32(0xF)) << np.uint32(4 * slot)
-                assert np.array_equal(words, want)
+                swz = np.arange(128)[None, :] ^ ((np.arange(16)[:, None] & 3) << 3)
+                assert np.array_equal(words, np.take_along_axis(want, swz, axis=1))
                 scales = blob[b + 8192:b + 9216].view(np.uint16).reshape(4, 128)
                 assert np.array_equal(scales, sc[e, kb * 4:(kb + 1) * 4, nb * 128:(nb + 1) * 128])
 
