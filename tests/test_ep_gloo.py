@@ -92,6 +92,8 @@ def _worker(rank, world, port, silu, balanced, q, mode="auto"):
         outs = [torch.empty((T // world) * TOPK, out.shape[1] * 2, dtype=torch.uint8)
                 for _ in range(world)]
         dist.all_gather(outs, out.view(torch.uint8))
+        # every rank has its copy before any rank tears its connections down
+        dist.barrier()
         if rank == 0:
             q.put(torch.cat(outs).view(torch.int16).numpy())
     except Exception as e:  # report instead of leaving the parent waiting
