@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (S > 1 && (size_t)tiles * S * unit_bytes > split.part_bytes) --S;
     }
     const int total = tiles * S;                  // work units: (tile, K split)
+    const bool few_units = total <= 4 * (int)gridDim.x;   // at most ~4 units per CTA
 
     if (warp == 0) {
         // ================= TMA producer =================
@@ -270,16 +271,67 @@ __global__ void __launch_bounds__(kThreads, 1)
             int e, row0, rows, nb;
             decode_tile<NT>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
             const int nl = (rows + kABox - 1) & ~(kABox - 1);
-            // stage this tile's scales: a_sc[kb][j], w_sc[g][kb]
-            if (!epi_sync()) break;
-            for (int i = et; i < nl * nk; i += kEpiThreads) {
-                const int j = i / nk, kb = i - j * nk;
-                a_sc[kb * NT + j] = (j < rows) ? __ldg(args.a_scale + (size_t)(row0 + j) * nk + kb) : 0.0f;
-            }
+            // stage this unit's scales, K blocks kb0..kb1 only: a_sc[kb - kb0][j],
+            // w_sc[g][kb - kb0].  With few units per CTA (small batches) the
+            // staging latency is exposed, so up to 8 loads per thread are in
+            // flight before their stores and the first batch is loaded before
+            // the rendezvous that frees the previous tile's copy; with many units
+            // per CTA the producer runs ahead of the epilogue and the plain loop
+            // measured faster (fewer registers and instructions).
+            const int nkb = kb1 - kb0;
+            const int n_as = nl * nkb;
             const size_t wsb = ((size_t)e * (N >> 7) + nb) * nk;
-            for (int i = et; i < nk; i += kEpiThreads) {
-                w_sc[i] = __ldg(args.w_scale + wsb + i);
-                if (PAIR) w_sc[nk + i] = __ldg(args.w_scale + wsb + (size_t)(N >> 8) * nk + i);
+            if (few_units) {
+                auto load_batch = [&](int base, float (&v)[8]) {
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) {
+                        const int i = base + x * kEpiThreads;
+                        const int j = i / nkb, kb = kb0 + (i - j * nkb);
+                        v[x] = (i < n_as && j < rows)
+                                   ? __ldg(args.a_scale + (size_t)(row0 + j) * nk + kb)
+                                   : 0.0f;
+                    }
+                };
+                auto store_batch = [&](int base, const float (&v)[8]) {
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) {
+                        const int i = base + x * kEpiThreads;
+                        const int j = i / nkb;
+                        if (i < n_as) a_sc[(i - j * nkb) * NT + j] = v[x];
+                    }
+                };
+                float v0[8];
+                load_batch(et, v0);
+                const float w0 = et < nkb ? __ldg(args.w_scale + wsb + kb0 + et) : 0.0f;
+                const float w1 = (PAIR && et < nkb)
+                                     ? __ldg(args.w_scale + wsb + (size_t)(N >> 8) * nk + kb0 + et)
+                                     : 0.0f;
+                if (!epi_sync()) break;
+                store_batch(et, v0);
+                for (int base = et + 8 * kEpiThreads; base < n_as; base += 8 * kEpiThreads) {
+                    float v[8];
+                    load_batch(base, v);
+                    store_batch(base, v);
+                }
+                if (et < nkb) {
+                    w_sc[et] = w0;
+                    if (PAIR) w_sc[nk + et] = w1;
+                }
+            } else {
+                if (!epi_sync()) break;
+                for (int i = et; i < n_as; i += kEpiThreads) {
+                    const int j = i / nkb, kb = kb0 + (i - j * nkb);
+                    a_sc[(kb - kb0) * NT + j] =
+                        (j < rows) ? __ldg(args.a_scale + (size_t)(row0 + j) * nk + kb) : 0.0f;
+                }
+                if (et < nkb) {
+                    w_sc[et] = __ldg(args.w_scale + wsb + kb0 + et);
+                    if (PAIR) w_sc[nk + et] = __ldg(args.w_scale + wsb + (size_t)(N >> 8) * nk + kb0 + et);
+                }
+            }
+            for (int i = et + kEpiThreads; i < nkb; i += kEpiThreads) {
+                w_sc[i] = __ldg(args.w_scale + wsb + kb0 + i);
+                if (PAIR) w_sc[nk + i] = __ldg(args.w_scale + wsb + (size_t)(N >> 8) * nk + kb0 + i);
             }
             if (!epi_sync()) break;
 
@@ -298,9 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * C::kCols;
-                const float ws = w_sc[kb];
-                const float wsu = PAIR ? w_sc[nk + kb] : 0.0f;
-                const float* asc = a_sc + kb * NT;
+                const float ws = w_sc[kb - kb0];
+                const float wsu = PAIR ? w_sc[nk + kb - kb0] : 0.0f;
+                const float* asc = a_sc + (kb - kb0) * NT;
 #pragma unroll
                 for (int c = 0; c < NT; c += 16) {
                     if (c >= nl) break;                  // columns past the tile's MMA N

@@ -66,19 +66,19 @@ __device__ __forceinline__ __nv_bfloat16* out_row_ptr(const GemmArgs& a, int oro
     return a.out + (size_t)orow * ldo;
 }
 
-// One K block of the prefill epilogue: this thread's row of the 256-column
-// TMEM partial at `tb` (columns [c0, c0 + CPH) of each 128-column half, the
-// thread's column group) scaled into its accumulators, acc0 for the first
-// weight block (s0 = a_scale * w_scale[block 0]) and acc1 for the second (s1).
+// One K block of the prefill epilogue: this thread's row of the 2*HALF-column
+// TMEM partial at `tb` (CPH columns of each half, the thread's column group)
+// scaled into its accumulators, acc0 for the first half's weight rows
+// (s0 = a_scale * w_scale[their block]) and acc1 for the second's (s1).
 // The caller waits for the partial (tfull) before and releases the buffer after.
-template <int CPH, int LD>
+template <int CPH, int LD, int HALF = 128>
 __device__ __forceinline__ void promote_kblock(uint32_t tb, float (&acc0)[CPH], float (&acc1)[CPH],
                                                float s0, float s1) {
 #pragma unroll
     for (int c = 0; c < CPH; c += LD) {
         float v[LD], u[LD];
         tmem_ld_cols<LD>(tb + c, v);
-        tmem_ld_cols<LD>(tb + 128 + c, u);
+        tmem_ld_cols<LD>(tb + HALF + c, u);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < LD; j += 2) {
@@ -88,15 +88,15 @@ __device__ __forceinline__ void promote_kblock(uint32_t tb, float (&acc0)[CPH], 
     }
 }
 
-// Stores one row of a finished prefill tile: the thread's CPH columns of each
-// weight block, as bf16 (16-byte stores), at output row `o`, output tile nb,
-// column group h.  PAIR (SiLU): silu(gate) * up of the two blocks into 128
-// output columns per tile; otherwise both blocks side by side (256 columns).
-template <bool PAIR, int CPH>
+// Stores one row of a finished prefill tile (2*HALF weight rows) as bf16
+// (16-byte stores) at output row `o`, output tile nb, column group h: the
+// thread's CPH columns of each half.  PAIR (SiLU): silu(gate) * up of the two
+// halves into HALF output columns per tile; otherwise both halves side by side.
+template <bool PAIR, int CPH, int HALF = 128>
 __device__ __forceinline__ void store_tile_row(__nv_bfloat16* o, int nb, int h,
                                                const float (&acc0)[CPH], const float (&acc1)[CPH]) {
     if (PAIR) {
-        uint4* dst = reinterpret_cast<uint4*>(o + nb * 128 + h * CPH);
+        uint4* dst = reinterpret_cast<uint4*>(o + nb * HALF + h * CPH);
 #pragma unroll
         for (int c = 0; c < CPH; c += 8) {
             uint4 pk;
@@ -111,8 +111,8 @@ __device__ __forceinline__ void store_tile_row(__nv_bfloat16* o, int nb, int h,
             dst[c >> 3] = pk;
         }
     } else {
-        uint4* d0 = reinterpret_cast<uint4*>(o + nb * 256 + h * CPH);
-        uint4* d1 = reinterpret_cast<uint4*>(o + nb * 256 + 128 + h * CPH);
+        uint4* d0 = reinterpret_cast<uint4*>(o + nb * 2 * HALF + h * CPH);
+        uint4* d1 = reinterpret_cast<uint4*>(o + nb * 2 * HALF + HALF + h * CPH);
 #pragma unroll
         for (int c = 0; c < CPH; c += 8) {
             uint4 p0, p1;
@@ -280,6 +280,46 @@ constexpr int kPpStage = 128 * 128 + 128 * 128;    // A half 16 KB + B half 16 K
 constexpr int kPpMaxStages = 6;
 constexpr int kPpEpiWarps = kPfEpiWarps;    // CTA-pair form: the single-CTA form's warp roles
 constexpr int kPpThreads = kPfThreads;
+constexpr int kPpBN = 256;                   // its weight rows per pair tile (256 or 128)
+
+// CTA-pair tile of 256 tokens x BN weight rows: each CTA loads 128 token rows
+// and BN/2 weight rows per 128-wide K block and holds a 128 x BN fp32 partial
+// per K block in Tensor Memory (512 / BN buffers).
+template <int BN>
+struct PpTile {
+    static constexpr int kB = (BN / 2) * 128;            // this CTA's weight rows x 128 bytes
+    static constexpr int kStage = 128 * 128 + kB;        // A 16 KB + B 16 or 8 KB
+    static constexpr int kBufs = 512 / BN;
+    static constexpr int kMaxStages = BN == 256 ? 6 : 9;
+};
+
+struct Pp2Layout {
+    int stages_off, segs_off, segc_off, mts_off, part_off, bar_off, misc_off, total;
+};
+
+template <int BN>
+__host__ __device__ inline Pp2Layout pp2_layout(int stages, int E) {
+    using T = PpTile<BN>;
+    Pp2Layout L;
+    int o = 0;
+    L.stages_off = o;
+    o += T::kStage * stages;
+    L.segs_off = o;
+    o += 4 * E;
+    L.segc_off = o;
+    o += 4 * E;
+    L.mts_off = o;
+    o += 4 * (E + 1);
+    L.part_off = o;
+    o += 4 * (kPpThreads + 1);
+    o = (o + 7) & ~7;
+    L.bar_off = o;
+    o += 8 * (2 * T::kMaxStages + 2 * T::kBufs + 1);
+    L.misc_off = o;
+    o += 16;
+    L.total = o;
+    return L;
+}
 
 enum : int { SITE_PEER_EMPTY = 9, SITE_PEER_TAIL = 10 };
 

@@ -458,35 +458,37 @@ __global__ void __launch_bounds__(kPfPeerThreads, 1)
 //     while the other still reads its shared memory or writes its Tensor Memory.
 // ---------------------------------------------------------------------------
 
-template <bool PAIR>
+template <bool PAIR, int BN>
 __global__ void __launch_bounds__(kPpThreads, 1)
     fp8_w13_prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_w,
                                 const __grid_constant__ CUtensorMap tm_a, const GemmArgs args) {
     pdl_begin();
+    using T = PpTile<BN>;
+    constexpr int kHalf = BN / 2;                  // weight rows per CTA = partial columns per half
     constexpr int kEW = kPpEpiWarps;
     constexpr int kEpi0 = kPfEpi0;
-    constexpr int kCPH = 512 / kEW;
+    constexpr int kCPH = kHalf / (kEW / 4);        // columns per thread in each half
     constexpr int kLD = kCPH < kPfLdCols ? kCPH : kPfLdCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = args.M, N = args.N, K = args.K, E = args.E, NS = args.stages;
     const int nk = K >> 7;
-    const int nbc = N >> 8;
+    const int nbc = N / BN;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const PpLayout L = pp_layout(NS, E);
+    const Pp2Layout L = pp2_layout<BN>(NS, E);
     int* seg_s = reinterpret_cast<int*>(smem + L.segs_off);
     int* seg_c = reinterpret_cast<int*>(smem + L.segc_off);
     int* mt_start = reinterpret_cast<int*>(smem + L.mts_off);
     int* part = reinterpret_cast<int*>(smem + L.part_off);
     const uint32_t bar0 = smem_addr(smem + L.bar_off);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (kPpMaxStages + s); };
-    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + a); };
-    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPpMaxStages + 2 + a); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * kPpMaxStages + 4);
+    auto empty_bar = [&](int s) { return bar0 + 8u * (T::kMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * T::kMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * T::kMaxStages + T::kBufs + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * T::kMaxStages + 2 * T::kBufs);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
     const uint32_t stage_base = smem_addr(smem + L.stages_off);
@@ -496,7 +498,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
             mbar_init(full_bar(s), 1);            // the leader's arm; bytes from both CTAs
             mbar_init(empty_bar(s), 1);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < T::kBufs; ++a) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), 2 * kEW);   // one per epilogue warp of both CTAs
         }
@@ -550,10 +552,10 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                 int e, row0, rows, nb;
                 decode_tile<256>(t, nbc, E, mt_start, seg_s, seg_c, e, row0, rows, nb);
                 const bool a_live = 128 * (int)rank < rows;      // this CTA's A rows exist
-                const uint32_t bytes = 3 * 16384 + (rows > 128 ? 16384 : 0);
+                const uint32_t bytes = 16384 + 2 * T::kB + (rows > 128 ? 16384 : 0);
                 const int arow = row0 + 128 * (int)rank;
-                const int wrow = PAIR ? e * N + (rank ? (N >> 1) : 0) + nb * 128
-                                      : e * N + nb * 256 + 128 * (int)rank;
+                const int wrow = PAIR ? e * N + (rank ? (N >> 1) : 0) + nb * kHalf
+                                      : e * N + nb * BN + kHalf * (int)rank;
                 for (int kb = 0; kb < nk; ++kb, ++it, rp.advance(NS)) {
                     const int s = rp.slot;
                     if (!mbar_wait_cl(empty_bar(s), rp.phase ^ 1u, abort_flag, args.ctl,
@@ -562,7 +564,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                         break;
                     }
                     if (leader) mbar_expect_tx(full_bar(s), bytes);
-                    const uint32_t dst = stage_base + s * kPpStage;
+                    const uint32_t dst = stage_base + s * T::kStage;
                     const uint32_t bar = mapa_shared(full_bar(s), 0);
                     if (a_live) tma_load_2d_pair(dst, &tm_a, kb * 128, arow, bar, pol);
                     tma_load_2d_pair(dst + 16384, &tm_w, kb * 128, wrow, bar, pol);
@@ -579,11 +581,11 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     auto mma_issuer = [&]() {
         // ================= MMA issuer (leader CTA) =================
         if (leader && elect_one()) {
-            constexpr uint32_t idesc = make_idesc(256, 256, 0, 0);
+            constexpr uint32_t idesc = make_idesc(256, BN, 0, 0);
             RingPos rs, ra;
             bool ok = true;
             for (int t = pair; t < total && ok; t += npairs) {
-                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(2)) {
+                for (int kb = 0; kb < nk; ++kb, rs.advance(NS), ra.advance(T::kBufs)) {
                     const int s = rs.slot, a = ra.slot;
                     if (!mbar_wait_cl(tempty_bar(a), ra.phase ^ 1u, abort_flag, args.ctl,
                                       SITE_TEMPTY) ||
@@ -592,8 +594,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = stage_base + s * kPpStage;
-                    const uint32_t d = tmem_base + a * 256;
+                    const uint32_t st = stage_base + s * T::kStage;
+                    const uint32_t d = tmem_base + a * BN;
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
                         mma_f8f6f4_pair(d, sdesc_k_sw128(st + ks * 32),
@@ -623,8 +625,10 @@ __global__ void __launch_bounds__(kPpThreads, 1)
             const int my_rows = min(max(rows - 128 * (int)rank, 0), 128);
             const bool live = r < my_rows;
             const float* as_row = args.a_scale + (size_t)(my0 + (live ? r : 0)) * nk;
-            const int blk0 = PAIR ? nb : 2 * nb;
-            const int blk1 = PAIR ? (N >> 8) + nb : 2 * nb + 1;
+            // 128-row weight blocks of the two halves' rows (one block for both
+            // halves when BN = 128 without SiLU)
+            const int blk0 = (PAIR ? nb * kHalf : nb * BN) >> 7;
+            const int blk1 = (PAIR ? (N >> 1) + nb * kHalf : nb * BN + kHalf) >> 7;
             const float* ws0 = args.w_scale + ((size_t)e * (N >> 7) + blk0) * nk;
             const float* ws1 = args.w_scale + ((size_t)e * (N >> 7) + blk1) * nk;
             float acc0[kCPH], acc1[kCPH];
@@ -634,7 +638,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                 acc1[j] = 0.0f;
             }
             bool ok = true;
-            for (int kb = 0; kb < nk; ++kb, ra.advance(2)) {
+            for (int kb = 0; kb < nk; ++kb, ra.advance(T::kBufs)) {
                 const float sa = live ? __ldg(as_row + kb) : 0.0f;
                 const float s0 = sa * __ldg(ws0 + kb), s1 = sa * __ldg(ws1 + kb);
                 ok = __all_sync(0xffffffffu, mbar_wait_cl(tfull_bar(ra.slot), ra.phase, abort_flag,
@@ -642,8 +646,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
                 if (my_rows > 0)
-                    promote_kblock<kCPH, kLD>(tmem_base + lane_addr + ra.slot * 256 + h * kCPH,
-                                              acc0, acc1, s0, s1);
+                    promote_kblock<kCPH, kLD, kHalf>(tmem_base + lane_addr + ra.slot * BN + h * kCPH,
+                                                     acc0, acc1, s0, s1);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(ra.slot), 0));
@@ -655,7 +659,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                 if (orow < 0 || orow >= args.out_total) orow = -1;
             }
             if (live && orow >= 0)
-                store_tile_row<PAIR, kCPH>(args.out + (size_t)orow * ldo, nb, h, acc0, acc1);
+                store_tile_row<PAIR, kCPH, kHalf>(args.out + (size_t)orow * ldo, nb, h, acc0, acc1);
         }
     };
 
@@ -684,22 +688,24 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     }
 }
 
-template <bool PAIR>
+template <bool PAIR, int BN = kPpBN>
 int launch_fp8_prefill_pairs_p(const DeviceInfo* info, const void* a, const float* a_scale,
                                const void* w, const float* w_scale, void* out, const int32_t* seg,
                                int seg_pairs, int M, int N, int K, int E, cudaStream_t stream,
                                const OutMap& om) {
+    using T = PpTile<BN>;
+    if (N % BN) return FERRET_ERR_SHAPE;
     CUtensorMap tm_w, tm_a;
     int rc = make_tmap_2d(&tm_w, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, K, 128,
-                          128, true);
+                          BN / 2, true);
     if (rc != FERRET_OK) return rc;
     rc = make_tmap_2d(&tm_a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, 128, 128, true);
     if (rc != FERRET_OK) return rc;
     const int budget = info->max_smem_optin - 1024;
-    const int stages = std::min(kPpMaxStages, (budget - pp_layout(0, E).total) / kPpStage);
+    const int stages = std::min(T::kMaxStages, (budget - pp2_layout<BN>(0, E).total) / T::kStage);
     if (stages < 2) return FERRET_ERR_SHAPE;
-    const int smem = pp_layout(stages, E).total + 1024;
-    auto kern = fp8_w13_prefill_pair_kernel<PAIR>;
+    const int smem = pp2_layout<BN>(stages, E).total + 1024;
+    auto kern = fp8_w13_prefill_pair_kernel<PAIR, BN>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
         cudaGetLastError();
         return FERRET_ERR_CUDA;

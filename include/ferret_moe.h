@@ -54,10 +54,11 @@ extern "C" {
                                        the tensor-core MMA (kind::mxf8f6f4.block_scale) from
                                        their exponent bits; other launches keep the exact-scale
                                        kernels (exact for such scales) */
-#define FERRET_PREFILL_PAIRS 0x4    /* 128-token-tile launches: each expert's whole 256-row chunks
-                                       on CTA pairs (tcgen05.mma.cta_group::2, 256x256 tiles),
-                                       the rest on single CTAs (with FERRET_UE8M0_SCALES: the
-                                       block-scaled pair kernel); same results, measured slower */
+#define FERRET_PREFILL_PAIRS 0x4    /* 128-token-tile launches on CTA pairs
+                                       (tcgen05.mma.cta_group::2, 256-token x 256-row tiles over
+                                       every expert's rows; with FERRET_UE8M0_SCALES the
+                                       block-scaled pair kernel on whole 256-row chunks, the rest
+                                       on single CTAs); same results, measured slower */
 
 /* Library version (FERRET_MOE_VERSION). */
 FERRET_API int ferret_version(void);
@@ -274,8 +275,9 @@ FERRET_API int ferret_fp8_grouped_gemm_nt_contiguous_noalloc(
  * One-time (load-time) repack of raw compressed-tensors INT4 W13 weights and
  * their scales into the blob ferret_int4_moe_w13 reads: for every expert,
  * 128-row n block and 128-wide K block, 9216 contiguous bytes = 2048 int32
- * words [k/8][n] (the 8 nibbles of each word reordered to K offsets
- * {0,2,4,6,1,3,5,7}) followed by the 4 x 128 bf16 group scales [k/32][n].
+ * words [k/8][n ^ 8 (k/8 mod 4)] (the 8 nibbles of each word reordered to K
+ * offsets {0,2,4,6,1,3,5,7}; the XOR spreads the kernels' shared-memory reads
+ * over all banks) followed by the 4 x 128 bf16 group scales [k/32][n].
  * The one-time pre-permutation the reference contract allows
  * (tasks/kimi-moe-w13-int4-grouped-gemm.yaml:69-71); it replaces the Marlin
  * repack gptq_marlin_moe_repack (baselines/kimi-moe-w13-int4/baseline_marlin.py:80-82).
