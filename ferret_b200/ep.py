@@ -80,18 +80,45 @@ def contiguous_placement(E: int, G: int) -> torch.Tensor:
 
 
 def balanced_placement(counts: torch.Tensor, G: int) -> torch.Tensor:
-    """Greedy LPT with exactly E/G experts per rank: experts by descending load,
-    each to the least-loaded rank that still has room.  Returns the owner-order
-    table (the experts of rank 0, then rank 1, ...)."""
+    """Expert placement with exactly E/G experts per rank that minimises the
+    busiest rank's routed rows.  Greedy LPT first (experts by descending load,
+    each to the least-loaded rank that still has room), then pairwise swaps:
+    while some swap of an expert of the busiest rank with a lighter expert of
+    another rank lowers the larger of the two ranks' loads below the current
+    maximum, take the best one.  Under skewed routing one expert can hold most
+    of a rank's share; LPT then fills its rank with mid-sized experts, and the
+    swaps trade them for the smallest ones.  Returns the owner-order table
+    (the experts of rank 0, then rank 1, ...)."""
     E = counts.numel()
     per = E // G
-    order = torch.argsort(counts.to(torch.int64), descending=True, stable=True).tolist()
+    c = [int(x) for x in counts.tolist()]
+    order = sorted(range(E), key=lambda e: -c[e])          # stable: ties by expert id
     load = [0] * G
     slots = [[] for _ in range(G)]
     for e in order:
         r = min((g for g in range(G) if len(slots[g]) < per), key=lambda g: (load[g], g))
         slots[r].append(e)
-        load[r] += int(counts[e])
+        load[r] += c[e]
+    while G > 1:
+        m = max(range(G), key=lambda g: (load[g], -g))
+        best = None
+        for i, a in enumerate(slots[m]):
+            for r in range(G):
+                if r == m:
+                    continue
+                for j, b in enumerate(slots[r]):
+                    d = c[a] - c[b]
+                    if d <= 0:
+                        continue
+                    new_max = max(load[m] - d, load[r] + d)
+                    if new_max < load[m] and (best is None or new_max < best[0]):
+                        best = (new_max, i, r, j, d)
+        if best is None:
+            break
+        _, i, r, j, d = best
+        slots[m][i], slots[r][j] = slots[r][j], slots[m][i]
+        load[m] -= d
+        load[r] += d
     return torch.tensor([e for s in slots for e in sorted(s)], dtype=torch.int32)
 
 

@@ -126,6 +126,20 @@ def test_ep_matches_single_process(world, silu, balanced, mode):
     assert not ref[0].any()          # the dropped pair is a zero row
 
 
+def test_balanced_placement_pairs_a_dominant_expert_with_the_smallest():
+    """Skewed routing: one expert holds most of a rank's share.  With E/G
+    experts per rank its rank's load can be no lower than that expert plus the
+    E/G - 1 smallest ones; the placement reaches that bound (greedy LPT alone
+    gives the dominant expert's rank mid-sized experts)."""
+    from ferret_b200.ep import balanced_placement
+    counts = torch.tensor([1000, 1, 1, 1, 1, 1, 1, 1, 300, 300, 300, 300, 10, 10, 10, 10])
+    G, per = 4, 4
+    table = balanced_placement(counts, G)
+    assert sorted(table.tolist()) == list(range(16))
+    loads = [int(counts[table[g * per:(g + 1) * per].long()].sum()) for g in range(G)]
+    assert max(loads) == 1000 + 1 + 1 + 1
+
+
 def test_balanced_placement_evens_load():
     from ferret_b200.ep import balanced_placement
     counts = torch.tensor([100, 1, 1, 1, 50, 50, 2, 2])
