@@ -126,18 +126,17 @@ def test_ep_matches_single_process(world, silu, balanced, mode):
     assert not ref[0].any()          # the dropped pair is a zero row
 
 
-def test_balanced_placement_pairs_a_dominant_expert_with_the_smallest():
-    """Skewed routing: one expert holds most of a rank's share.  With E/G
-    experts per rank its rank's load can be no lower than that expert plus the
-    E/G - 1 smallest ones; the placement reaches that bound (greedy LPT alone
-    gives the dominant expert's rank mid-sized experts)."""
+def test_balanced_placement_reaches_the_optimum_lpt_misses():
+    """Skewed (Zipf-like) loads where greedy LPT leaves the busiest rank at 1004
+    rows; the best split into two ranks of four experts has 986 (by exhaustive
+    search: {399, 247, 215, 125} against {594, 204, 112, 70}).  The pairwise
+    swaps after LPT reach it."""
     from ferret_b200.ep import balanced_placement
-    counts = torch.tensor([1000, 1, 1, 1, 1, 1, 1, 1, 300, 300, 300, 300, 10, 10, 10, 10])
-    G, per = 4, 4
-    table = balanced_placement(counts, G)
-    assert sorted(table.tolist()) == list(range(16))
-    loads = [int(counts[table[g * per:(g + 1) * per].long()].sum()) for g in range(G)]
-    assert max(loads) == 1000 + 1 + 1 + 1
+    counts = torch.tensor([594, 399, 247, 215, 204, 125, 112, 70])
+    table = balanced_placement(counts, 2)
+    assert sorted(table.tolist()) == list(range(8))
+    loads = [int(counts[table[:4].long()].sum()), int(counts[table[4:].long()].sum())]
+    assert max(loads) == 986
 
 
 def test_balanced_placement_evens_load():
