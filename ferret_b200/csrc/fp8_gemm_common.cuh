@@ -71,7 +71,9 @@ __device__ __forceinline__ __nv_bfloat16* out_row_ptr(const GemmArgs& a, int oro
 // scaled into its accumulators, acc0 for the first half's weight rows
 // (s0 = a_scale * w_scale[their block]) and acc1 for the second's (s1).
 // The caller waits for the partial (tfull) before and releases the buffer after.
-template <int CPH, int LD, int HALF = 128>
+// PACKED: one fma.rn.f32x2 per two columns, else one fmaf per column (the same
+// roundings; which is faster depends on the kernel around it).
+template <int CPH, int LD, int HALF = 128, bool PACKED = true>
 __device__ __forceinline__ void promote_kblock(uint32_t tb, float (&acc0)[CPH], float (&acc1)[CPH],
                                                float s0, float s1) {
 #pragma unroll
@@ -82,8 +84,15 @@ __device__ __forceinline__ void promote_kblock(uint32_t tb, float (&acc0)[CPH], 
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < LD; j += 2) {
-            ffma2(acc0[c + j], acc0[c + j + 1], v[j], v[j + 1], s0);
-            ffma2(acc1[c + j], acc1[c + j + 1], u[j], u[j + 1], s1);
+            if constexpr (PACKED) {
+                ffma2(acc0[c + j], acc0[c + j + 1], v[j], v[j + 1], s0);
+                ffma2(acc1[c + j], acc1[c + j + 1], u[j], u[j + 1], s1);
+            } else {
+                acc0[c + j] = fmaf(v[j], s0, acc0[c + j]);
+                acc0[c + j + 1] = fmaf(v[j + 1], s0, acc0[c + j + 1]);
+                acc1[c + j] = fmaf(u[j], s1, acc1[c + j]);
+                acc1[c + j + 1] = fmaf(u[j + 1], s1, acc1[c + j + 1]);
+            }
         }
     }
 }

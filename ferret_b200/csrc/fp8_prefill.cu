@@ -190,7 +190,9 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), kEW);      // one arrive per epilogue warp
+            // single-GPU form: one arrive per epilogue warp; EP form: one per
+            // epilogue thread (each measured faster in its own kernel)
+            mbar_init(tempty_bar(a), EP ? kEW * 32 : kEW);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -336,13 +338,18 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap* tm_w, const CUte
                                                        args.ctl, SITE_TFULL));
                 if (!ok) break;
                 tc_fence_after();
-                promote_kblock<kCPH, kLD>(tmem_base + lane_addr + ra.slot * 256 + h * kCPH, acc0,
-                                          acc1, s0, s1);
-                // every lane's loads of this buffer are complete (wait::ld)
-                // before the warp's single arrive releases it to the MMA
+                promote_kblock<kCPH, kLD, 128, !EP>(tmem_base + lane_addr + ra.slot * 256 + h * kCPH,
+                                                    acc0, acc1, s0, s1);
+                // this thread's loads of the buffer are complete (wait::ld)
+                // before it releases the buffer to the MMA: each thread (EP), or
+                // the warp once all its lanes have (single-GPU form)
                 tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(tempty_bar(ra.slot));
+                if constexpr (EP) {
+                    mbar_arrive(tempty_bar(ra.slot));
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty_bar(ra.slot));
+                }
             }
             if (!ok) break;
             int orow = row0 + r;
