@@ -67,7 +67,7 @@ constexpr int kRdPart = 16;                 // fp32 partials per thread (4 accum
 constexpr int kRdCtas = 3;                  // CTAs per SM
 constexpr int kRdMaxStages = 8;
 
-enum : int { RD_EMPTY = 1, RD_FULL = 2, RD_DRAIN = 3 };
+enum : int { RD_EMPTY = 1, RD_FULL = 2, RD_DRAIN = 3, RD_SPLIT = 4 };
 
 struct Int4DecArgs {
     const uint8_t* blob;                    // repacked blobs [E][N/128][K/128] x kRdBlob
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kRdThreads, kRdCtas)
     uint8_t* ring = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     __shared__ int it_start[kRdMaxE + 1];
     __shared__ int scan_part[kRdThreads + 1];
-    __shared__ __align__(8) uint64_t bars[2 * kRdMaxStages];
+    __shared__ __align__(8) uint64_t bars[2 * kRdMaxStages + 1];
     __shared__ int s_last;
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kRdThreads, kRdCtas)
     const uint32_t bar0 = smem_addr(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kRdMaxStages + s); };
+    const uint32_t split_bar = bar0 + 8u * (2 * kRdMaxStages);   // math-thread rendezvous
     volatile int* abort_flag = &s_abort;
 
     if (tid == 0) {
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(kRdThreads, kRdCtas)
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), kRdWarps);
         }
+        mbar_init(split_bar, kRdMath);
         s_abort = 0;
         mbar_init_fence();
     }
@@ -221,6 +223,15 @@ __global__ void __launch_bounds__(kRdThreads, kRdCtas)
     const int s_off = 8192 + ((wrow >> 1) * 4);
     const int x_off = kW * kRdBlob + g * 256 + t * 16;
     RingPos rs;
+    uint32_t split_phase = 0;
+    // rendezvous of the math threads (split-K): bounded and abort-aware, so a
+    // warp that gave up on a wait never strands the others
+    auto math_sync = [&]() -> bool {
+        mbar_arrive(split_bar);
+        const bool ok = mbar_wait(split_bar, split_phase & 1u, abort_flag, args.ctl, RD_SPLIT);
+        ++split_phase;
+        return __all_sync(0xffffffffu, ok);
+    };
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const RdUnit w = rd_unit(u, S, E, nob, nk, it_start, args.offsets);
         float ag0[4] = {0, 0, 0, 0}, ag1[4] = {0, 0, 0, 0};
@@ -268,9 +279,9 @@ __global__ void __launch_bounds__(kRdThreads, kRdCtas)
                 }
             }
             __threadfence();
-            named_bar_sync(1, kRdMath);
+            if (!math_sync()) break;
             if (tid == 0) s_last = atomicAdd(args.cnt + w.item, 1) == S - 1;
-            named_bar_sync(1, kRdMath);
+            if (!math_sync()) break;
             if (!s_last) continue;
             __threadfence();
 #pragma unroll
